@@ -1,0 +1,146 @@
+/*
+ * pmkl_b200.h -- C ABI of the B200 (sm_100a) causal-attention and
+ * warp-softmax library (libpmkl_b200.so).
+ *
+ * This is the drop-in boundary for pmkl's hot path.  Every pointer argument
+ * is a DEVICE pointer owned by the caller; the library never allocates device
+ * memory on these entry points and never synchronises: work is enqueued on the
+ * caller's CUDA stream (`stream`, a cudaStream_t; NULL = legacy default
+ * stream) and the call returns once it is enqueued.
+ *
+ * Every entry point returns PMKL_OK (0) on success or a negative pmkl_status;
+ * pmkl_status_string() names it.  Argument errors are detected on the host
+ * before anything is launched, mirroring the reference's CHECK_FAIL
+ * (pmkl/core/utils/exception.h:121-129) and TORCH_CHECK
+ * (pmkl_pytorch_ext/fused_self_attention.cpp:140-141) checks.
+ */
+#ifndef PMKL_B200_H_
+#define PMKL_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PMKL_B200_VERSION 100 /* 1.0.0 */
+
+/* Element types.  The reference dispatches float, double, half and bfloat16
+ * (fused_self_attention.cpp:152-156); double is rejected here. */
+typedef enum pmkl_dtype {
+    PMKL_DTYPE_F32 = 0,
+    PMKL_DTYPE_F16 = 1,
+    PMKL_DTYPE_BF16 = 2,
+} pmkl_dtype;
+
+typedef enum pmkl_status {
+    PMKL_OK = 0,
+    PMKL_ERR_INVALID_SHAPE = -1,   /* negative / inconsistent sizes, size limits */
+    PMKL_ERR_INVALID_DTYPE = -2,   /* unknown or unsupported dtype combination */
+    PMKL_ERR_NULL_POINTER = -3,    /* a required pointer is NULL for a non-empty problem */
+    PMKL_ERR_MISALIGNED = -4,      /* a pointer breaks the alignment the chosen kernel needs */
+    PMKL_ERR_UNSUPPORTED = -5,     /* valid arguments this build has no kernel for */
+    PMKL_ERR_NO_DEVICE = -6,       /* no CUDA device, or not an sm_100 device */
+    PMKL_ERR_LAUNCH = -7,          /* the CUDA runtime rejected the launch */
+    PMKL_ERR_DEVICE_TIMEOUT = -8,  /* a kernel gave up on a bounded wait (see pmkl_device_error) */
+} pmkl_status;
+
+/* Kernel selection for pmkl_causal_attention_fwd_ex. */
+typedef enum pmkl_attention_kernel {
+    PMKL_ATTN_AUTO = 0,    /* tcgen05 path when it applies, else the SIMT path */
+    PMKL_ATTN_SIMT = 1,    /* generic CUDA-core kernel: any dtype, head size 1..256 */
+    PMKL_ATTN_TCGEN05 = 2, /* tensor-core kernel: fp16/bf16, head size 64 or 128 */
+} pmkl_attention_kernel;
+
+/*
+ * Fused (causal) self-attention forward.
+ *
+ * Replaces pmkl::nlp::causal_attention_forward<scalar_t, BLOCK_M, HIDDEN_SIZE>
+ * (pmkl/nlp/causal_attention.h:258-288) and the compute behind
+ * fused_self_attention_fw (pmkl_pytorch_ext/fused_self_attention.cpp:139-173).
+ *
+ *   q, k, v, o : [batch, heads, seq, hidden], contiguous, element type `dtype`
+ *                for q/k/v and `out_dtype` for o.
+ *   m, l       : [batch, heads, seq], element type `out_dtype`.
+ *                m = row max of the scaled, masked scores  s = scale * q.k
+ *                l = sum over keys of exp(s - m)
+ *                o = softmax(s) v
+ *                (semantics of fused_self_attention.cpp:38-61 and
+ *                 causal_attention.h:200-255).
+ *   is_causal  : key j is visible to query i only when j <= i.
+ *   scale      : score scale; pass 0 (or any value <= 0) for 1/sqrt(hidden),
+ *                the value the reference hard-codes (causal_attention.h:192).
+ *   dtype      : PMKL_DTYPE_F32, _F16 or _BF16.
+ *   out_dtype  : dtype (the reference's behaviour: outputs in v's dtype,
+ *                fused_self_attention.cpp:148-150) or PMKL_DTYPE_F32.
+ *
+ * Any seq >= 0 is accepted (the reference kernel needs seq % 32 == 0,
+ * causal_attention.h:267; its CPU path takes any seq).  An empty problem
+ * returns PMKL_OK without launching (causal_attention.h:270).
+ */
+int pmkl_causal_attention_fwd(const void *q, const void *k, const void *v, void *o, void *m, void *l,
+                              int batch, int heads, int seq, int hidden, int dtype, int out_dtype,
+                              int is_causal, float scale, void *stream);
+
+/* As pmkl_causal_attention_fwd, with an explicit kernel choice (tests and
+ * benchmarks use it to run one path on purpose).  PMKL_ATTN_TCGEN05 returns
+ * PMKL_ERR_UNSUPPORTED when that kernel does not cover the arguments. */
+int pmkl_causal_attention_fwd_ex(const void *q, const void *k, const void *v, void *o, void *m, void *l,
+                                 int batch, int heads, int seq, int hidden, int dtype, int out_dtype,
+                                 int is_causal, float scale, int kernel, void *stream);
+
+/*
+ * Row-wise softmax / log-softmax.
+ *
+ * Replaces pmkl::norm::warp_softmax_forward<output_t, input_t, acc_t,
+ * is_log_softmax> (pmkl/norm/warp_softmax.h:159-201).  Same argument meaning:
+ * `rows` rows of `elements` values, consecutive rows `stride` elements apart;
+ * dst uses the same row stride.  Accumulation is fp32 (acc_t = float).
+ * 0 <= elements <= 1024 as in the reference (warp_softmax.h:162); elements == 0
+ * returns without launching.  Rows whose exp-sum is zero produce NaN
+ * (warp_softmax.h:147-148).
+ */
+int pmkl_warp_softmax_fwd(void *dst, const void *src, int elements, int stride, int rows, int in_dtype,
+                          int out_dtype, int is_log, void *stream);
+
+/* Human-readable name of a pmkl_status value (static storage). */
+const char *pmkl_status_string(int status);
+
+/* PMKL_B200_VERSION of the loaded library. */
+int pmkl_version(void);
+
+/* Waits for `stream` (NULL = legacy default stream).  The C++ shim calls it
+ * after each launch to keep the reference launcher's synchronous behaviour
+ * (pmkl/core/launcher/cuda_launcher.h:334, stream_sync).  Returns PMKL_OK,
+ * or PMKL_ERR_LAUNCH when the stream reports an error. */
+int pmkl_stream_synchronize(void *stream);
+
+/*
+ * Device-side error word of the current device: bit 0 set when a kernel gave
+ * up on a bounded wait and returned early (its outputs are then undefined).
+ * This call synchronises the device.  Returns PMKL_OK when the word is zero,
+ * PMKL_ERR_DEVICE_TIMEOUT when it is set (and clears it when `clear` != 0),
+ * or PMKL_ERR_LAUNCH when the runtime reports an error.  No reference
+ * counterpart: the reference's launcher only checks launch errors
+ * (pmkl/core/launcher/cuda_launcher.h:297-335).
+ */
+int pmkl_device_error(int clear);
+
+/*
+ * Tensor-core self-test: runs the tile primitives of the tcgen05 kernel in
+ * isolation on one CTA and writes fp32 results for comparison with a host
+ * matrix product.  Diagnostic only; no reference counterpart.
+ *   which == 0:  c[128 x 128] = a[128 x hidden] * b[128 x hidden]^T
+ *                (both operands K-major, the Q.K^T form)
+ *   which == 1:  c[128 x hidden] = a[128 x 128] * b[128 x hidden]
+ *                (a staged through tensor memory, b MN-major: the P.V form)
+ * a, b: fp16/bf16 (`dtype`), row-major, contiguous; hidden is 64 or 128.
+ */
+int pmkl_tc_selftest(int which, const void *a, const void *b, float *c, int hidden, int dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PMKL_B200_H_ */

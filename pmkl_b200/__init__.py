@@ -1,0 +1,115 @@
+"""pmkl_b200 -- B200 (sm_100a) implementation of pmkl's fused causal
+self-attention and warp-softmax path.
+
+Layers, bottom up:
+
+* ``libpmkl_b200.so`` (``csrc/``): the CUDA kernels behind the C ABI of
+  ``include/pmkl_b200.h``;
+* ``pmkl_pytorch_ext`` / ``pmkl_function`` (``torch_ext/``): the reference's
+  torch extension and autograd wrapper, same names and signatures, calling the
+  C ABI on the current CUDA stream;
+* this module: locates the built artefacts, puts the torch binding on
+  ``sys.path`` so that ``import pmkl_pytorch_ext`` and
+  ``from pmkl_function import fused_self_attention`` work as they do with the
+  reference installed, and offers a ctypes view of the C ABI (``capi()``).
+
+The library must be built (``python -m pmkl_b200.build``); nothing here falls
+back to another implementation when it is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import sys
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "lib" / "libpmkl_b200.so"
+EXT_DIR = PKG_DIR / "torch_ext" / "_build"
+FUNCTION_DIR = PKG_DIR / "torch_ext"
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
+PMKL_OK = 0
+
+for _p in (EXT_DIR, FUNCTION_DIR):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+_capi = None
+
+
+class PmklError(RuntimeError):
+    """A pmkl_status other than PMKL_OK, raised by the ctypes helpers."""
+
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what} failed: {capi().pmkl_status_string(status).decode()}")
+
+
+def capi() -> ctypes.CDLL:
+    """The C ABI (include/pmkl_b200.h) through ctypes.  Raises if the library
+    has not been built: there is no fallback path."""
+    global _capi
+    if _capi is None:
+        if not LIB_PATH.is_file():
+            raise ImportError(f"libpmkl_b200.so is not built ({LIB_PATH}); run python -m pmkl_b200.build")
+        L = ctypes.CDLL(str(LIB_PATH))
+        vp, i32, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+        L.pmkl_causal_attention_fwd.restype = i32
+        L.pmkl_causal_attention_fwd.argtypes = [vp] * 6 + [i32] * 7 + [f32, vp]
+        L.pmkl_causal_attention_fwd_ex.restype = i32
+        L.pmkl_causal_attention_fwd_ex.argtypes = [vp] * 6 + [i32] * 7 + [f32, i32, vp]
+        L.pmkl_warp_softmax_fwd.restype = i32
+        L.pmkl_warp_softmax_fwd.argtypes = [vp, vp] + [i32] * 6 + [vp]
+        L.pmkl_status_string.restype = ctypes.c_char_p
+        L.pmkl_status_string.argtypes = [i32]
+        L.pmkl_version.restype = i32
+        L.pmkl_version.argtypes = []
+        L.pmkl_stream_synchronize.restype = i32
+        L.pmkl_stream_synchronize.argtypes = [vp]
+        L.pmkl_device_error.restype = i32
+        L.pmkl_device_error.argtypes = [i32]
+        L.pmkl_tc_selftest.restype = i32
+        L.pmkl_tc_selftest.argtypes = [i32, vp, vp, vp, i32, i32, vp]
+        _capi = L
+    return _capi
+
+
+def torch_dtype_code(dtype) -> int:
+    import torch
+
+    return {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}[dtype]
+
+
+def _stream_ptr(stream) -> int:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def attention_fwd(q, k, v, o, m, l, is_causal: bool, scale: float = 0.0, kernel: int = KERNEL_AUTO,
+                  stream=None) -> None:
+    """Calls pmkl_causal_attention_fwd_ex on caller-allocated torch CUDA
+    tensors (q, k, v, o: [B, H, S, D]; m, l: [B, H, S]).  Raises PmklError."""
+    B, H, S, D = q.shape
+    rc = capi().pmkl_causal_attention_fwd_ex(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), m.data_ptr(), l.data_ptr(),
+        B, H, S, D, torch_dtype_code(q.dtype), torch_dtype_code(o.dtype), int(bool(is_causal)), float(scale),
+        int(kernel), _stream_ptr(stream))
+    if rc != PMKL_OK:
+        raise PmklError(rc, "pmkl_causal_attention_fwd")
+
+
+def warp_softmax_fwd(dst, src, elements: int, stride: int, rows: int, is_log: bool = False, stream=None) -> None:
+    """Calls pmkl_warp_softmax_fwd on caller-allocated torch CUDA tensors."""
+    rc = capi().pmkl_warp_softmax_fwd(dst.data_ptr(), src.data_ptr(), int(elements), int(stride), int(rows),
+                                      torch_dtype_code(src.dtype), torch_dtype_code(dst.dtype), int(bool(is_log)),
+                                      _stream_ptr(stream))
+    if rc != PMKL_OK:
+        raise PmklError(rc, "pmkl_warp_softmax_fwd")
+
+
+def device_error(clear: bool = True) -> int:
+    """pmkl_device_error: synchronises the device, returns the status."""
+    return capi().pmkl_device_error(int(bool(clear)))

@@ -1,0 +1,381 @@
+// pmkl_b200.cu -- C ABI of libpmkl_b200 (declared in include/pmkl_b200.h):
+// argument checks, kernel selection, TMA descriptor set-up and launches.
+//
+// Host-side behaviour follows the reference's entry points:
+//   pmkl::nlp::causal_attention_forward   pmkl/nlp/causal_attention.h:258-288
+//   fused_self_attention_fw               pmkl_pytorch_ext/fused_self_attention.cpp:139-173
+//   pmkl::norm::warp_softmax_forward      pmkl/norm/warp_softmax.h:159-201
+// but never synchronises (the reference launcher syncs after every launch,
+// pmkl/core/launcher/cuda_launcher.h:334) and never resets the device (the
+// reference's launcher does at start-up, cuda_launcher.h:149,273).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+
+#include "attention_simt.cuh"
+#include "attention_tc.cuh"
+#include "common.cuh"
+#include "pmkl_b200.h"
+#include "softmax.cuh"
+
+namespace pmkl_b200 {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// ------------------------------------------------------------------ device checks
+struct DeviceState {
+    std::once_flag once;
+    bool ok = false;
+};
+DeviceState g_dev[kMaxDevices];
+
+int current_device_ok() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return PMKL_ERR_NO_DEVICE;
+    }
+    if (dev < 0 || dev >= kMaxDevices) return PMKL_ERR_NO_DEVICE;
+    DeviceState &st = g_dev[dev];
+    std::call_once(st.once, [&]() {
+        int major = 0, minor = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) == cudaSuccess) {
+            st.ok = (major == 10 && minor == 0);  // code is built for sm_100a only
+        } else {
+            cudaGetLastError();
+        }
+    });
+    return st.ok ? PMKL_OK : PMKL_ERR_NO_DEVICE;
+}
+
+// Sets a kernel's dynamic shared-memory limit once per device.
+template <typename K>
+bool ensure_smem(K kernel, int bytes, std::once_flag (&flags)[kMaxDevices]) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    bool ok = true;
+    std::call_once(flags[dev], [&]() {
+        ok = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+    });
+    return ok;
+}
+
+int launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? PMKL_OK : PMKL_ERR_LAUNCH;
+}
+
+// ------------------------------------------------------------------ TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = []() -> EncodeTiledFn {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// [planes, rows, cols] 16-bit tensor, 128-row x 64-column boxes, 128-byte swizzle.
+bool make_tile_map(CUtensorMap *map, const void *base, int dtype, int cols, int rows, long long planes) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const CUtensorMapDataType dt =
+        dtype == PMKL_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(planes)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2,
+                                   static_cast<cuuint64_t>(cols) * 2 * static_cast<cuuint64_t>(rows)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(tc::kBoxCols), 128u, 1u};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return enc(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ attention launchers
+template <int D, bool BF16>
+int launch_tc(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int BH, int causal,
+              float scale, int dtype, int out_dtype, cudaStream_t stream) {
+    using C = tc::Cfg<D>;
+    static std::once_flag smem_once[kMaxDevices];
+    auto kernel = tc::attn_fwd_tc_kernel<D, BF16>;
+    if (!ensure_smem(kernel, C::kSmemBytes, smem_once)) return PMKL_ERR_LAUNCH;
+    CUtensorMap tq, tk, tv, to;
+    const bool o16 = out_dtype != PMKL_DTYPE_F32;
+    if (!make_tile_map(&tq, q, dtype, D, S, BH) || !make_tile_map(&tk, k, dtype, D, S, BH) ||
+        !make_tile_map(&tv, v, dtype, D, S, BH) || !make_tile_map(&to, o16 ? o : q, dtype, D, S, BH))
+        return PMKL_ERR_LAUNCH;
+    tc::Params p;
+    p.S = S;
+    p.BH = BH;
+    p.n_qt = (S + tc::kBM - 1) / tc::kBM;
+    p.causal = causal;
+    p.out_dtype = out_dtype;
+    p.scale = scale;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.o_f32 = o;
+    p.m_out = m;
+    p.l_out = l;
+    const long long blocks = static_cast<long long>(p.n_qt) * BH;
+    if (blocks > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    kernel<<<static_cast<unsigned>(blocks), tc::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+    return launch_status();
+}
+
+template <typename T, int DMAX>
+int launch_simt_t(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int D, int BH,
+                  int causal, float scale, int out_dtype, cudaStream_t stream) {
+    static std::once_flag smem_once[kMaxDevices];
+    auto kernel = simt::attn_fwd_simt_kernel<T, DMAX>;
+    constexpr int smem = simt::smem_bytes<DMAX>();
+    if (!ensure_smem(kernel, smem, smem_once)) return PMKL_ERR_LAUNCH;
+    const int n_qt = (S + simt::kBM - 1) / simt::kBM;
+    const long long blocks = static_cast<long long>(n_qt) * BH;
+    if (blocks > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    kernel<<<static_cast<unsigned>(blocks), simt::kThreads, smem, stream>>>(
+        static_cast<const T *>(q), static_cast<const T *>(k), static_cast<const T *>(v), o, m, l, S, D, BH, n_qt,
+        causal, scale, out_dtype);
+    return launch_status();
+}
+
+template <typename T>
+int launch_simt(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int D, int BH,
+                int causal, float scale, int out_dtype, cudaStream_t stream) {
+    if (D <= 32) return launch_simt_t<T, 32>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
+    if (D <= 64) return launch_simt_t<T, 64>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
+    if (D <= 128) return launch_simt_t<T, 128>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
+    return launch_simt_t<T, 256>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
+}
+
+bool tc_applies(const void *q, const void *k, const void *v, const void *o, int D, int dtype, int out_dtype) {
+    if (dtype != PMKL_DTYPE_F16 && dtype != PMKL_DTYPE_BF16) return false;
+    if (D != 64 && D != 128) return false;
+    if (out_dtype != dtype && out_dtype != PMKL_DTYPE_F32) return false;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return false;
+    return true;
+}
+
+int attention_impl(const void *q, const void *k, const void *v, void *o, void *m, void *l, int batch, int heads,
+                   int seq, int hidden, int dtype, int out_dtype, int is_causal, float scale, int kernel,
+                   void *stream_) {
+    if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
+    if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
+    if (out_dtype != dtype && out_dtype != PMKL_DTYPE_F32) return PMKL_ERR_INVALID_DTYPE;
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05)
+        return PMKL_ERR_UNSUPPORTED;
+    const long long BH = static_cast<long long>(batch) * heads;
+    if (BH == 0 || seq == 0 || hidden == 0) return PMKL_OK;  // causal_attention.h:270
+    if (hidden > 256) return PMKL_ERR_UNSUPPORTED;
+    if (BH > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    if (!q || !k || !v || !o || !m || !l) return PMKL_ERR_NULL_POINTER;
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    const float sc = (scale > 0.f) ? scale : 1.0f / sqrtf(static_cast<float>(hidden));
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const int causal = is_causal ? 1 : 0;
+    const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype);
+    if (kernel == PMKL_ATTN_TCGEN05 && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if (kernel != PMKL_ATTN_SIMT && tc_ok) {
+        const int bh = static_cast<int>(BH);
+        if (dtype == PMKL_DTYPE_BF16)
+            return hidden == 64 ? launch_tc<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
+                                : launch_tc<128, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
+        return hidden == 64 ? launch_tc<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
+                            : launch_tc<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
+    }
+    const int bh = static_cast<int>(BH);
+    if (dtype == PMKL_DTYPE_F32)
+        return launch_simt<float>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, stream);
+    if (dtype == PMKL_DTYPE_F16)
+        return launch_simt<__half>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, stream);
+    return launch_simt<__nv_bfloat16>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, stream);
+}
+
+// ------------------------------------------------------------------ softmax launchers
+template <bool LOG>
+int launch_softmax_vec(float *dst, const float *src, int elements, int stride, int rows, cudaStream_t stream) {
+    const int vpl = (elements + 127) / 128;
+    const unsigned blocks = static_cast<unsigned>((rows + softmax::kThreads / 32 - 1) / (softmax::kThreads / 32));
+#define PMKL_SOFTMAX_VEC_CASE(N)                                                                     \
+    case N:                                                                                          \
+        softmax::softmax_vec_kernel<N, LOG><<<blocks, softmax::kThreads, 0, stream>>>(dst, src, elements, \
+                                                                                      stride, rows); \
+        break;
+    switch (vpl) {
+        PMKL_SOFTMAX_VEC_CASE(1)
+        PMKL_SOFTMAX_VEC_CASE(2)
+        PMKL_SOFTMAX_VEC_CASE(3)
+        PMKL_SOFTMAX_VEC_CASE(4)
+        PMKL_SOFTMAX_VEC_CASE(5)
+        PMKL_SOFTMAX_VEC_CASE(6)
+        PMKL_SOFTMAX_VEC_CASE(7)
+        PMKL_SOFTMAX_VEC_CASE(8)
+        default:
+            return PMKL_ERR_INVALID_SHAPE;
+    }
+#undef PMKL_SOFTMAX_VEC_CASE
+    return launch_status();
+}
+
+template <bool LOG>
+int launch_softmax_gen(void *dst, const void *src, int elements, int stride, int rows, int in_dtype, int out_dtype,
+                       cudaStream_t stream) {
+    int l2e = 0;
+    while ((1 << l2e) < elements) ++l2e;  // log2_ceil, warp_softmax.h:25-29
+    const int lanes = (1 << l2e) < 32 ? (1 << l2e) : 32;
+    const long long rows_per_block = static_cast<long long>(softmax::kThreads / 32) * (32 / lanes);
+    const unsigned blocks = static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block);
+#define PMKL_SOFTMAX_GEN_CASE(L)                                                                           \
+    case L:                                                                                                \
+        softmax::softmax_gen_kernel<L, LOG><<<blocks, softmax::kThreads, 0, stream>>>(dst, src, elements, \
+                                                                                      stride, rows, in_dtype, \
+                                                                                      out_dtype);        \
+        break;
+    switch (l2e) {
+        PMKL_SOFTMAX_GEN_CASE(0)
+        PMKL_SOFTMAX_GEN_CASE(1)
+        PMKL_SOFTMAX_GEN_CASE(2)
+        PMKL_SOFTMAX_GEN_CASE(3)
+        PMKL_SOFTMAX_GEN_CASE(4)
+        PMKL_SOFTMAX_GEN_CASE(5)
+        PMKL_SOFTMAX_GEN_CASE(6)
+        PMKL_SOFTMAX_GEN_CASE(7)
+        PMKL_SOFTMAX_GEN_CASE(8)
+        PMKL_SOFTMAX_GEN_CASE(9)
+        PMKL_SOFTMAX_GEN_CASE(10)
+        default:
+            return PMKL_ERR_INVALID_SHAPE;
+    }
+#undef PMKL_SOFTMAX_GEN_CASE
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace pmkl_b200
+
+using namespace pmkl_b200;
+
+extern "C" {
+
+int pmkl_causal_attention_fwd(const void *q, const void *k, const void *v, void *o, void *m, void *l, int batch,
+                              int heads, int seq, int hidden, int dtype, int out_dtype, int is_causal, float scale,
+                              void *stream) {
+    return attention_impl(q, k, v, o, m, l, batch, heads, seq, hidden, dtype, out_dtype, is_causal, scale,
+                          PMKL_ATTN_AUTO, stream);
+}
+
+int pmkl_causal_attention_fwd_ex(const void *q, const void *k, const void *v, void *o, void *m, void *l, int batch,
+                                 int heads, int seq, int hidden, int dtype, int out_dtype, int is_causal, float scale,
+                                 int kernel, void *stream) {
+    return attention_impl(q, k, v, o, m, l, batch, heads, seq, hidden, dtype, out_dtype, is_causal, scale, kernel,
+                          stream);
+}
+
+int pmkl_warp_softmax_fwd(void *dst, const void *src, int elements, int stride, int rows, int in_dtype,
+                          int out_dtype, int is_log, void *stream_) {
+    if (elements < 0 || elements > 1024) return PMKL_ERR_INVALID_SHAPE;  // warp_softmax.h:162
+    if (rows < 0 || stride < elements) return PMKL_ERR_INVALID_SHAPE;
+    if (!dtype_valid(in_dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
+    if (elements == 0 || rows == 0) return PMKL_OK;  // warp_softmax.h:163-164
+    if (!dst || !src) return PMKL_ERR_NULL_POINTER;
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const bool vec = in_dtype == PMKL_DTYPE_F32 && out_dtype == PMKL_DTYPE_F32 && (elements % 4) == 0 &&
+                     (stride % 4) == 0 && aligned16(dst) && aligned16(src);
+    if (vec) {
+        return is_log ? launch_softmax_vec<true>(static_cast<float *>(dst), static_cast<const float *>(src), elements,
+                                                 stride, rows, stream)
+                      : launch_softmax_vec<false>(static_cast<float *>(dst), static_cast<const float *>(src),
+                                                  elements, stride, rows, stream);
+    }
+    return is_log ? launch_softmax_gen<true>(dst, src, elements, stride, rows, in_dtype, out_dtype, stream)
+                  : launch_softmax_gen<false>(dst, src, elements, stride, rows, in_dtype, out_dtype, stream);
+}
+
+const char *pmkl_status_string(int status) {
+    switch (status) {
+        case PMKL_OK:
+            return "PMKL_OK";
+        case PMKL_ERR_INVALID_SHAPE:
+            return "PMKL_ERR_INVALID_SHAPE: invalid or unsupported sizes";
+        case PMKL_ERR_INVALID_DTYPE:
+            return "PMKL_ERR_INVALID_DTYPE: unsupported dtype";
+        case PMKL_ERR_NULL_POINTER:
+            return "PMKL_ERR_NULL_POINTER: null pointer for a non-empty problem";
+        case PMKL_ERR_MISALIGNED:
+            return "PMKL_ERR_MISALIGNED: pointer alignment";
+        case PMKL_ERR_UNSUPPORTED:
+            return "PMKL_ERR_UNSUPPORTED: no kernel for these arguments";
+        case PMKL_ERR_NO_DEVICE:
+            return "PMKL_ERR_NO_DEVICE: no sm_100 CUDA device is current";
+        case PMKL_ERR_LAUNCH:
+            return "PMKL_ERR_LAUNCH: CUDA launch failed";
+        case PMKL_ERR_DEVICE_TIMEOUT:
+            return "PMKL_ERR_DEVICE_TIMEOUT: a kernel abandoned a bounded wait";
+        default:
+            return "PMKL_ERR_UNKNOWN";
+    }
+}
+
+int pmkl_version(void) { return PMKL_B200_VERSION; }
+
+int pmkl_stream_synchronize(void *stream) {
+    return cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) == cudaSuccess ? PMKL_OK : PMKL_ERR_LAUNCH;
+}
+
+int pmkl_device_error(int clear) {
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    if (cudaDeviceSynchronize() != cudaSuccess) return PMKL_ERR_LAUNCH;
+    unsigned int word = 0;
+    if (cudaMemcpyFromSymbol(&word, g_device_error, sizeof(word)) != cudaSuccess) return PMKL_ERR_LAUNCH;
+    if (word != 0 && clear) {
+        const unsigned int zero = 0;
+        if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess) return PMKL_ERR_LAUNCH;
+    }
+    return word ? PMKL_ERR_DEVICE_TIMEOUT : PMKL_OK;
+}
+
+int pmkl_tc_selftest(int which, const void *a, const void *b, float *c, int hidden, int dtype, void *stream_) {
+    if (which != 0 && which != 1) return PMKL_ERR_UNSUPPORTED;
+    if (hidden != 64 && hidden != 128) return PMKL_ERR_UNSUPPORTED;
+    if (dtype != PMKL_DTYPE_F16 && dtype != PMKL_DTYPE_BF16) return PMKL_ERR_INVALID_DTYPE;
+    if (!a || !b || !c) return PMKL_ERR_NULL_POINTER;
+    if (!aligned16(a) || !aligned16(b)) return PMKL_ERR_MISALIGNED;
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    CUtensorMap ta, tb;
+    if (!make_tile_map(&ta, a, dtype, which == 0 ? hidden : 128, 128, 1) ||
+        !make_tile_map(&tb, b, dtype, hidden, 128, 1))
+        return PMKL_ERR_LAUNCH;
+    constexpr int smem = 4 * tc::kBoxBytes + 1024 + 64;
+    const bool bf = dtype == PMKL_DTYPE_BF16;
+    auto run = [&](auto kernel) -> int {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return PMKL_ERR_LAUNCH;
+        kernel<<<1, 128, smem, stream>>>(ta, tb, static_cast<const uint16_t *>(a), c, which);
+        return launch_status();
+    };
+    if (hidden == 64) return bf ? run(tc::tc_selftest_kernel<64, true>) : run(tc::tc_selftest_kernel<64, false>);
+    return bf ? run(tc::tc_selftest_kernel<128, true>) : run(tc::tc_selftest_kernel<128, false>);
+}
+
+}  // extern "C"

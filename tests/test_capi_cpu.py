@@ -1,0 +1,111 @@
+"""CPU-side checks of the drop-in boundary: the C-ABI library loads and
+exports every function include/pmkl_b200.h declares, argument errors are
+reported before any device work, the C++ shim compiles, and the torch binding
+imports and rejects CPU tensors.  No kernel runs here."""
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+import torch
+
+import pmkl_b200
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "pmkl_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(pmkl_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for n in ("pmkl_causal_attention_fwd", "pmkl_warp_softmax_fwd", "pmkl_status_string"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    L = pmkl_b200.capi()
+    for name in declared_functions():
+        assert hasattr(L, name), f"{name} declared in pmkl_b200.h but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(pmkl_b200.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (pmkl_\w+)", out))
+    assert set(declared_functions()) <= exported
+
+
+def test_version_and_status_strings():
+    L = pmkl_b200.capi()
+    assert L.pmkl_version() == 100
+    assert L.pmkl_status_string(0) == b"PMKL_OK"
+    for code in range(-1, -9, -1):
+        assert L.pmkl_status_string(code).startswith(b"PMKL_ERR_")
+    assert L.pmkl_status_string(-99) == b"PMKL_ERR_UNKNOWN"
+
+
+# Argument errors are detected on the host before the device is touched, so
+# these calls are valid without a GPU (pointers are never dereferenced).
+FAKE = 0x10000  # non-null, 16-byte aligned, never dereferenced
+
+
+def attn(L, B=1, H=1, S=8, D=64, dtype=2, out_dtype=2, kernel=0, ptrs=FAKE):
+    return L.pmkl_causal_attention_fwd_ex(ptrs, ptrs, ptrs, ptrs, ptrs, ptrs, B, H, S, D, dtype, out_dtype, 1, 0.0,
+                                          kernel, None)
+
+
+def test_attention_argument_errors():
+    L = pmkl_b200.capi()
+    assert attn(L, B=-1) == -1
+    assert attn(L, S=-5) == -1
+    assert attn(L, dtype=7) == -2
+    assert attn(L, dtype=1, out_dtype=2) == -2  # out dtype must be the input dtype or fp32
+    assert attn(L, kernel=9) == -5
+    assert attn(L, D=257) == -5
+    assert attn(L, ptrs=0) == -3
+
+
+def test_attention_empty_problem_is_ok_without_device():
+    L = pmkl_b200.capi()
+    assert attn(L, B=0, ptrs=0) == 0
+    assert attn(L, S=0, ptrs=0) == 0
+    assert attn(L, H=0, ptrs=0) == 0
+
+
+def test_softmax_argument_errors():
+    L = pmkl_b200.capi()
+    f = L.pmkl_warp_softmax_fwd
+    assert f(FAKE, FAKE, 1025, 1025, 4, 0, 0, 0, None) == -1  # warp_softmax.h:162
+    assert f(FAKE, FAKE, -1, 8, 4, 0, 0, 0, None) == -1
+    assert f(FAKE, FAKE, 16, 8, 4, 0, 0, 0, None) == -1  # stride < elements
+    assert f(FAKE, FAKE, 16, 16, -1, 0, 0, 0, None) == -1
+    assert f(FAKE, FAKE, 16, 16, 4, 5, 0, 0, None) == -2
+    assert f(0, 0, 0, 0, 4, 0, 0, 0, None) == 0  # elements == 0: nothing to do
+    assert f(0, 0, 16, 16, 0, 0, 0, 0, None) == 0
+    assert f(0, FAKE, 16, 16, 4, 0, 0, 0, None) == -3
+
+
+def test_cpp_shim_compiles():
+    import torch.utils.cpp_extension as cpp
+
+    cuda_inc = Path(cpp.CUDA_HOME or "/usr/local/cuda") / "include"
+    subprocess.run(["g++", "-std=c++17", "-fsyntax-only", f"-I{REPO / 'include'}", f"-I{cuda_inc}",
+                    str(REPO / "tests" / "cpp" / "shim_test.cpp")], check=True)
+
+
+def test_torch_binding_imports_and_rejects_cpu():
+    import pmkl_pytorch_ext
+    from pmkl_function import fused_self_attention
+
+    q = torch.randn(1, 2, 8, 64)
+    with pytest.raises(NotImplementedError):
+        fused_self_attention(q, q, q, True)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pmkl_pytorch_ext.fused_self_attention_fw(q, q, q, True)
+    with pytest.raises(RuntimeError, match="shapes must match"):
+        pmkl_pytorch_ext.fused_self_attention_fw(q, q[:, :1], q, True)
+    with pytest.raises(RuntimeError, match="shapes must match"):
+        pmkl_pytorch_ext.fused_self_attention_fw(q[0], q[0], q[0], True)
+    assert pmkl_pytorch_ext.KERNEL_TCGEN05 == pmkl_b200.KERNEL_TCGEN05
