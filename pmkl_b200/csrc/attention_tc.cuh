@@ -133,7 +133,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_pfull, 4);
         mbar_init(bar_odone, 1);
         mbar_init(bar_final, 1);
-        *abort_flag = 0;
+        // Fast fail: once any CTA has abandoned a wait (the device error word
+        // is set), later CTAs skip their work instead of each timing out.
+        *abort_flag = (*reinterpret_cast<volatile unsigned int *>(&g_device_error) != 0u) ? 1 : 0;
         fence_mbarrier_init();
     }
     if (warp == 5) {
@@ -144,8 +146,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const bool skip = *abort_flag != 0;
 
-    if (warp == 4) {
+    if (skip) {
+        // nothing: fall through to the teardown
+    } else if (warp == 4) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             tma_prefetch_desc(&tm_q);
@@ -398,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
-    if (threadIdx.x == 0 && *abort_flag) report_device_error(PMKL_DEVERR_TIMEOUT);
+    if (threadIdx.x == 0 && *abort_flag && !skip) report_device_error(PMKL_DEVERR_TIMEOUT);
 }
 
 // ---------------------------------------------------------------------------
