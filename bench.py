@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--kernel", type=int, default=0,
+                    help="pmkl_attention_kernel value for the device-timed leg (0 = automatic choice)")
     return ap.parse_args()
 
 
@@ -346,7 +348,7 @@ def run_attention(args, wl, rank, world, local):
     stream = torch.cuda.current_stream()
 
     def step():
-        pmkl_b200.attention_fwd(q, k, v, o, m, l, causal, stream=stream)
+        pmkl_b200.attention_fwd(q, k, v, o, m, l, causal, kernel=args.kernel, stream=stream)
 
     sampler = ClockSampler(world, (not args.no_clocks) and rank == 0)
     total_ms, per_ms = timed_loop(step, args.steps, args.warmup, world)

@@ -1,0 +1,547 @@
+// attention_pp.cuh -- persistent, two-query-tile ("ping-pong") tcgen05 flash
+// attention forward for sm_100a: fp16/bf16 inputs, head size 64 or 128.
+//
+// Same results as pmkl::nlp::causal_attention_forward
+// (pmkl/nlp/causal_attention.h:145-256): O (normalised), m = row max of the
+// scaled masked scores, l = sum exp(s - m).  Organisation:
+//
+//   * persistent grid (one CTA per SM); a work unit is a pair of adjacent
+//     128-row query tiles A, B of one (batch*head) slice.  Units are taken
+//     round-robin from a list sorted by decreasing causal work (longest first).
+//   * warp roles (16 warps, 4 warpgroups):
+//       WG0  softmax of tile A        WG1  softmax of tile B
+//       WG2  epilogue (O/l -> 16-bit -> shared -> TMA store; m, l stores)
+//       WG3  warp 12: TMA loads (Q_A, Q_B per unit; K, V through a ring)
+//            warp 13: tcgen05.mma issue (one thread)
+//   * tensor memory: S_A [0,128) S_B [128,256) O_A [256,256+D) O_B [384,384+D).
+//     The softmax writes P (16-bit) into the upper half of its S buffer and,
+//     for tiles whose rows see at most 128 keys, the low part of a hi/lo split
+//     into the lower half; O += P V reads P from tensor memory.
+//   * the MMA thread issues, per key tile j:  PV_A(j), S_A(j+1), PV_B(j),
+//     S_B(j+1).  tcgen05.mma operations of one thread execute in issue order,
+//     so S_X(j+1) (which overwrites P_X(j)) runs after PV_X(j) has read it, and
+//     the commit that announces S_X(j+1) also proves PV_X(j) complete, which
+//     frees O_X for the softmax's rescale.  While softmax A works on S_A(j+1)
+//     the tensor pipe runs PV_B(j) and S_B(j+1), and the other way round.
+//   * the O rescale after a max change is skipped unless the running max grew
+//     by more than 2^8 (the stale max stays the exp2 reference point; the
+//     epilogue corrects m and l once).
+//   * every wait is bounded (sm100_ptx.cuh); on expiry the CTA drains its own
+//     copies and MMAs, frees tensor memory and reports PMKL_DEVERR_TIMEOUT.
+#pragma once
+
+#include "attention_tc.cuh"
+
+namespace pmkl_b200 {
+namespace pp {
+
+using tc::kBoxBytes;
+using tc::kBoxCols;
+
+constexpr int kThreads = 512;
+constexpr int kWarpTma = 12;
+constexpr int kWarpMma = 13;
+constexpr uint32_t kTmemCols = 512;
+__host__ __device__ constexpr uint32_t col_s(int x) { return x ? 128u : 0u; }  // S_A, S_B
+__host__ __device__ constexpr uint32_t col_o(int x) { return x ? 384u : 256u; }  // O_A, O_B
+constexpr uint32_t kPHi = 64;  // P (hi) columns inside an S buffer
+constexpr uint32_t kPLo = 0;   // P (lo) columns inside an S buffer
+
+// Register budget per warpgroup after the split (launch: 512 x 128 = 65536).
+constexpr uint32_t kRegSoftmax = 168;
+constexpr uint32_t kRegEpilogue = 80;
+constexpr uint32_t kRegProducer = 88;
+static_assert(128 * (2 * kRegSoftmax + kRegEpilogue + kRegProducer) <= 65536, "register split exceeds the pool");
+constexpr int kLaunchRegs = 128;
+
+template <int D>
+struct Cfg {
+    static_assert(D == 64 || D == 128, "head size 64 or 128");
+    static constexpr int kBoxes = D / kBoxCols;
+    static constexpr int kTile = kBoxes * kBoxBytes;       // 128 rows x D x 2 bytes
+    static constexpr int kStages = (D == 64) ? 8 : 4;      // K/V ring (K and V alternate)
+    static constexpr int kOffQ = 0;                         // Q_A, Q_B
+    static constexpr int kOffStage = 2 * kTile;             // epilogue staging, one 128 x 64 box
+    static constexpr int kOffRing = kOffStage + kBoxBytes;
+    static constexpr int kOffStats = kOffRing + kStages * kTile;  // [2][128] x {m_used, m_true, l}
+    static constexpr int kOffBars = kOffStats + 2 * 128 * 3 * 4;
+    static constexpr int kNumBars = 4 + 2 * kStages + 2 + 2 + 2 + 2 + 2 + 2 + 3;
+    static constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct Params {
+    int S;
+    int BH;
+    int n_pairs;     // ceil(n_qt / 2)
+    int n_units;     // n_pairs * BH
+    int causal;
+    int out_dtype;
+    float scale;
+    float scale_log2;
+    void *o_f32;
+    void *m_out;
+    void *l_out;
+};
+
+struct Unit {
+    int bh;
+    int row0;     // first row of tile A
+    bool act[2];  // tile active (row0 of the tile < S)
+    int n[2];     // key tiles per query tile
+    int n_max;
+    bool hilo[2];
+};
+
+__device__ __forceinline__ Unit decode(const Params &p, int u) {
+    Unit w;
+    const int n_kv_all = (p.S + 127) / 128;
+    const int pair = p.causal ? (p.n_pairs - 1 - u / p.BH) : (u / p.BH);
+    w.bh = u % p.BH;
+    w.row0 = pair * 256;
+    for (int x = 0; x < 2; ++x) {
+        const int r0 = w.row0 + 128 * x;
+        w.act[x] = r0 < p.S;
+        w.n[x] = !w.act[x] ? 0 : (p.causal ? min(r0 / 128 + 1, n_kv_all) : n_kv_all);
+        w.hilo[x] = w.act[x] && w.n[x] == 1 && (p.causal ? (r0 == 0) : true);
+    }
+    w.n_max = max(w.n[0], w.n[1]);
+    return w;
+}
+
+// p = 2^(s * c2 - mref) for one 128-key score row, packed to 16-bit pairs and
+// stored into the P (hi) columns of the row's S buffer (and, with HILO, the
+// rounding remainder into the P (lo) columns).  Returns the fp32 row sum.
+template <bool BF16, bool HILO>
+__device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2, float mref, uint32_t sa) {
+    using namespace ptx;
+    float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    const float2 c22 = make_float2(c2, c2);
+    const float2 nm2 = make_float2(-mref, -mref);
+#pragma unroll
+    for (int c0 = 0; c0 < 128; c0 += 32) {
+        uint32_t ph[16];
+        uint32_t pl[HILO ? 16 : 1];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float2 a = fma2(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), c22, nm2);
+            const float2 e = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+            rs2[i & 3] = add2(rs2[i & 3], e);
+            ph[i] = pack2<BF16>(e.x, e.y);
+            if constexpr (HILO) {
+                float h0, h1;
+                tc::unpack2<BF16>(ph[i], h0, h1);
+                pl[i] = pack2<BF16>(e.x - h0, e.y - h1);
+            }
+        }
+        tmem_st16(sa + kPHi + c0 / 2, ph);
+        if constexpr (HILO) tmem_st16(sa + kPLo + c0 / 2, pl);
+    }
+    const float2 rr = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
+    return rr.x + rr.y;
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                       const Params p) {
+    using namespace ptx;
+    using C = Cfg<D>;
+    constexpr int NS = C::kStages;
+    constexpr int TILE = C::kTile;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t *sQ = smem + C::kOffQ;  // [2][TILE]
+    uint8_t *sStage = smem + C::kOffStage;
+    uint8_t *sRing = smem + C::kOffRing;  // [NS][TILE]
+    float *sStats = reinterpret_cast<float *>(smem + C::kOffStats);  // [2][3][128]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kOffBars);
+    uint64_t *q_full = bars;             // [2]
+    uint64_t *q_empty = bars + 2;        // [2]
+    uint64_t *kv_full = bars + 4;        // [NS]
+    uint64_t *kv_empty = kv_full + NS;   // [NS]
+    uint64_t *s_full = kv_empty + NS;    // [2]
+    uint64_t *p_full = s_full + 2;       // [2]
+    uint64_t *o_full = p_full + 2;       // [2]
+    uint64_t *o_empty = o_full + 2;      // [2]
+    uint64_t *st_full = o_empty + 2;     // [2]
+    uint64_t *st_empty = st_full + 2;    // [2]
+    uint64_t *mma_done = st_empty + 2;
+    uint64_t *stg_written = mma_done + 1;  // epilogue warps -> store thread
+    uint64_t *stg_free = stg_written + 1;  // store thread -> epilogue warps
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(stg_free + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int wg = warp >> 2;
+
+    if (threadIdx.x == 0) {
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(&q_full[x], 1);
+            mbar_init(&q_empty[x], 1);
+            mbar_init(&s_full[x], 1);
+            mbar_init(&p_full[x], 4);
+            mbar_init(&o_full[x], 1);
+            mbar_init(&o_empty[x], 4);
+            mbar_init(&st_full[x], 4);
+            mbar_init(&st_empty[x], 4);
+        }
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(mma_done, 1);
+        mbar_init(stg_written, 4);
+        mbar_init(stg_free, 1);
+        *abort_flag = (*reinterpret_cast<volatile unsigned int *>(&g_device_error) != 0u) ? 1 : 0;
+        fence_mbarrier_init();
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const bool skip = *abort_flag != 0;
+
+    if (wg == 3) {
+        reg_dealloc<kRegProducer>();
+        if (!skip && warp == kWarpTma && lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            tma_prefetch_desc(&tm_q);
+            tma_prefetch_desc(&tm_k);
+            tma_prefetch_desc(&tm_v);
+            int qc[2] = {0, 0};
+            int kvc = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+                const Unit w = decode(p, u);
+                for (int x = 0; x < 2 && ok; ++x) {
+                    if (!w.act[x]) continue;
+                    if (qc[x] > 0 && !(ok = mbar_wait(&q_empty[x], (qc[x] - 1) & 1, abort_flag))) break;
+                    mbar_arrive_expect_tx(&q_full[x], TILE);
+                    for (int b = 0; b < C::kBoxes; ++b)
+                        tma_load_3d(sQ + x * TILE + b * kBoxBytes, &tm_q, &q_full[x], b * kBoxCols, w.row0 + 128 * x,
+                                    w.bh);
+                    ++qc[x];
+                }
+                for (int j = 0; ok && j < w.n_max; ++j) {
+                    for (int kv = 0; kv < 2; ++kv) {
+                        const int s = kvc % NS;
+                        if (kvc >= NS && !(ok = mbar_wait(&kv_empty[s], ((kvc / NS) - 1) & 1, abort_flag))) break;
+                        mbar_arrive_expect_tx(&kv_full[s], TILE);
+                        const CUtensorMap *map = kv ? &tm_v : &tm_k;
+                        for (int b = 0; b < C::kBoxes; ++b)
+                            tma_load_3d(sRing + s * TILE + b * kBoxBytes, map, &kv_full[s], b * kBoxCols, j * 128, w.bh);
+                        ++kvc;
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // Let issued copies land before shared memory is released.
+                volatile int never = 0;
+                for (int i = max(0, kvc - NS); i < kvc; ++i) mbar_wait(&kv_full[i % NS], (i / NS) & 1, &never);
+                for (int x = 0; x < 2; ++x)
+                    if (qc[x] > 0) mbar_wait(&q_full[x], (qc[x] - 1) & 1, &never);
+            }
+        } else if (!skip && warp == kWarpMma && lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            constexpr uint32_t kIdescS = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+            constexpr uint32_t kIdescO = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
+            int qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+            int kvc = 0;
+            bool ok = true;
+            auto issue_s = [&](int x, uint32_t k_addr) {
+                const uint32_t q_addr = smem_u32(sQ + x * TILE);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tmem + col_s(x), smem_desc_sw128(q_addr + off, 16, 1024),
+                           smem_desc_sw128(k_addr + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&s_full[x]);
+            };
+            auto issue_pv = [&](int x, uint32_t v_addr, bool first, bool hilo) {
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, kBoxBytes, 1024);
+                    mma_ts(tmem + col_o(x), tmem + col_s(x) + kPHi + kk * 8, b, kIdescO, (!first || kk > 0) ? 1u : 0u);
+                }
+                if (hilo) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, kBoxBytes, 1024);
+                        mma_ts(tmem + col_o(x), tmem + col_s(x) + kPLo + kk * 8, b, kIdescO, 1u);
+                    }
+                }
+            };
+            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+                const Unit w = decode(p, u);
+                for (int x = 0; x < 2 && ok; ++x)
+                    if (w.act[x]) {
+                        ok = mbar_wait(&q_full[x], qc[x] & 1, abort_flag);
+                        ++qc[x];
+                    }
+                if (!ok) break;
+                // K_0 -> S_A(0), S_B(0)
+                int sK = kvc % NS;
+                if (!(ok = mbar_wait(&kv_full[sK], (kvc / NS) & 1, abort_flag))) break;
+                ++kvc;
+                tc_fence_after();
+                for (int x = 0; x < 2; ++x)
+                    if (w.act[x]) {
+                        issue_s(x, smem_u32(sRing + sK * TILE));
+                        if (w.n[x] == 1) mma_commit(&q_empty[x]);
+                    }
+                mma_commit(&kv_empty[sK]);
+                for (int j = 0; ok && j < w.n_max; ++j) {
+                    const int sV = kvc % NS;
+                    if (!(ok = mbar_wait(&kv_full[sV], (kvc / NS) & 1, abort_flag))) break;
+                    ++kvc;
+                    const bool has_next = j + 1 < w.n_max;
+                    int kvc_next = kvc;
+                    if (has_next) {
+                        sK = kvc % NS;
+                        ++kvc;
+                    }
+                    bool k_ready = false;
+                    for (int x = 0; x < 2 && ok; ++x) {
+                        if (j >= w.n[x]) continue;
+                        if (!(ok = mbar_wait(&p_full[x], pc[x] & 1, abort_flag))) break;
+                        ++pc[x];
+                        if (j == 0 && oc[x] > 0 && !(ok = mbar_wait(&o_empty[x], (oc[x] - 1) & 1, abort_flag))) break;
+                        tc_fence_after();
+                        issue_pv(x, smem_u32(sRing + sV * TILE), j == 0, w.hilo[x]);
+                        if (j + 1 < w.n[x]) {
+                            if (!k_ready) {
+                                if (!(ok = mbar_wait(&kv_full[sK], (kvc_next / NS) & 1, abort_flag))) break;
+                                k_ready = true;
+                                tc_fence_after();
+                            }
+                            issue_s(x, smem_u32(sRing + sK * TILE));
+                            if (j + 2 == w.n[x]) mma_commit(&q_empty[x]);
+                        } else {
+                            mma_commit(&o_full[x]);
+                            ++oc[x];
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(&kv_empty[sV]);
+                    if (has_next) mma_commit(&kv_empty[sK]);
+                }
+            }
+            // Drain every MMA issued before tensor memory is released.
+            mma_commit(mma_done);
+            volatile int never = 0;
+            mbar_wait(mma_done, 0, &never);
+        }
+    } else if (wg < 2) {
+        reg_alloc<kRegSoftmax>();
+        if (!skip) {
+            // ------------------------------------------------------------ softmax of tile x = wg
+            const int x = wg;
+            const int r_local = (warp & 3) * 32 + lane;  // == tensor-memory lane
+            const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+            const uint32_t sa = lane_base + col_s(x);
+            const float c2 = p.scale_log2;
+            int sc = 0, uc = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+                const Unit w = decode(p, u);
+                if (!w.act[x]) continue;
+                const int row = w.row0 + 128 * x + r_local;
+                float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
+                for (int j = 0; j < w.n[x]; ++j) {
+                    if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
+                    ++sc;
+                    tc_fence_after();
+                    float s[128];
+                    {
+                        uint32_t *sr = reinterpret_cast<uint32_t *>(s);
+                        tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                        tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                        tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+                        tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+                        tmem_wait_ld();
+                    }
+                    const int kbase = j * 128;
+                    int lim = p.S - kbase;
+                    if (p.causal) lim = min(lim, row - kbase + 1);
+                    if (lim < 128) {
+#pragma unroll
+                        for (int c = 0; c < 128; ++c)
+                            if (c >= lim) s[c] = -INFINITY;
+                    }
+                    float mx8[8];
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) mx8[t] = s[t];
+#pragma unroll
+                    for (int c = 8; c < 128; c += 8)
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[c + t]);
+                    const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                    m_true = fmaxf(m_true, mx);
+                    const bool resc =
+                        (m_used == -INFINITY) ? (m_true != -INFINITY) : ((m_true - m_used) * c2 > 8.0f);
+                    const float m_new = resc ? m_true : m_used;
+                    const float fac =
+                        resc ? ((m_used == -INFINITY) ? 0.f : ex2_approx((m_used - m_new) * c2)) : 1.f;
+                    const float mref = (m_new == -INFINITY) ? 0.f : m_new * c2;
+                    const float rsum = w.hilo[x] ? exp_pack_store<BF16, true>(s, c2, mref, sa)
+                                                 : exp_pack_store<BF16, false>(s, c2, mref, sa);
+                    // O_X is idle here: S_X(j) was issued after PV_X(j-1), and
+                    // its commit covers every earlier MMA.
+                    if (j > 0 && __any_sync(0xffffffffu, resc)) {
+#pragma unroll
+                        for (int cc = 0; cc < D / 32; ++cc) {
+                            uint32_t o[32];
+                            tmem_ld32(lane_base + col_o(x) + cc * 32, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * fac);
+                            tmem_st32(lane_base + col_o(x) + cc * 32, o);
+                        }
+                    }
+                    l = l * fac + rsum;
+                    m_used = m_new;
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&p_full[x]);
+                }
+                if (!ok) break;
+                // Row statistics for the epilogue.
+                if (uc > 0 && !(ok = mbar_wait_warp(&st_empty[x], (uc - 1) & 1, abort_flag))) break;
+                sStats[(x * 3 + 0) * 128 + r_local] = m_used;
+                sStats[(x * 3 + 1) * 128 + r_local] = m_true;
+                sStats[(x * 3 + 2) * 128 + r_local] = l;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&st_full[x]);
+                ++uc;
+            }
+        }
+    } else {
+        reg_dealloc<kRegEpilogue>();
+        if (!skip) {
+            // ------------------------------------------------------------ epilogue (WG2)
+            const int r_local = (warp & 3) * 32 + lane;
+            const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+            const bool lead = (warp == 8 && lane == 0);
+            const float c2 = p.scale_log2;
+            int oc[2] = {0, 0};
+            int nb = 0;  // staging boxes used so far
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+                const Unit w = decode(p, u);
+                for (int x = 0; x < 2 && ok; ++x) {
+                    if (!w.act[x]) continue;
+                    if (!(ok = mbar_wait_warp(&o_full[x], oc[x] & 1, abort_flag))) break;
+                    if (!(ok = mbar_wait_warp(&st_full[x], oc[x] & 1, abort_flag))) break;
+                    ++oc[x];
+                    tc_fence_after();
+                    const float m_used = sStats[(x * 3 + 0) * 128 + r_local];
+                    const float m_true = sStats[(x * 3 + 1) * 128 + r_local];
+                    const float l = sStats[(x * 3 + 2) * 128 + r_local];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&st_empty[x]);
+                    const float inv_l = 1.f / l;
+                    const int row = w.row0 + 128 * x + r_local;
+                    const uint32_t oa = lane_base + col_o(x);
+                    if (p.out_dtype == PMKL_DTYPE_F32) {
+                        float *orow = static_cast<float *>(p.o_f32) + (static_cast<size_t>(w.bh) * p.S + row) * D;
+#pragma unroll
+                        for (int cc = 0; cc < D / 32; ++cc) {
+                            uint32_t o[32];
+                            tmem_ld32(oa + cc * 32, o);
+                            tmem_wait_ld();
+                            if (cc == D / 32 - 1) {
+                                tc_fence_before();
+                                __syncwarp();
+                                if (lane == 0) mbar_arrive(&o_empty[x]);
+                            }
+                            if (row < p.S) {
+#pragma unroll
+                                for (int t = 0; t < 32; t += 4)
+                                    *reinterpret_cast<float4 *>(orow + cc * 32 + t) =
+                                        make_float4(__uint_as_float(o[t]) * inv_l, __uint_as_float(o[t + 1]) * inv_l,
+                                                    __uint_as_float(o[t + 2]) * inv_l,
+                                                    __uint_as_float(o[t + 3]) * inv_l);
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int b = 0; b < C::kBoxes; ++b) {
+                            // The staging box is free once the previous TMA store has read it.
+                            if (nb > 0 && !(ok = mbar_wait_warp(stg_free, (nb - 1) & 1, abort_flag))) break;
+                            uint8_t *box = sStage + r_local * 128;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                uint32_t o[32];
+                                tmem_ld32(oa + b * 64 + h * 32, o);
+                                tmem_wait_ld();
+                                if (b == C::kBoxes - 1 && h == 1) {
+                                    tc_fence_before();
+                                    __syncwarp();
+                                    if (lane == 0) mbar_arrive(&o_empty[x]);
+                                }
+                                uint32_t pk[16];
+#pragma unroll
+                                for (int t = 0; t < 16; ++t)
+                                    pk[t] = pack2<BF16>(__uint_as_float(o[2 * t]) * inv_l,
+                                                        __uint_as_float(o[2 * t + 1]) * inv_l);
+#pragma unroll
+                                for (int q4 = 0; q4 < 4; ++q4) {
+                                    const int chunk = h * 4 + q4;
+                                    *reinterpret_cast<uint4 *>(box + ((chunk ^ (r_local & 7)) * 16)) =
+                                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+                                }
+                            }
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(stg_written);
+                            if (lead) {
+                                // Once all four warps have written their rows of this box,
+                                // store it and hand the buffer back when the store has read it.
+                                if ((ok = mbar_wait(stg_written, nb & 1, abort_flag))) {
+                                    tma_store_3d(&tm_o, sStage, b * kBoxCols, w.row0 + 128 * x, w.bh);
+                                    tma_store_commit();
+                                    tma_store_wait_read0();
+                                }
+                                mbar_arrive(stg_free);
+                            }
+                            ++nb;
+                            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                            if (!ok) break;
+                        }
+                        if (!ok) break;
+                    }
+                    if (row < p.S) {
+                        const size_t idx = static_cast<size_t>(w.bh) * p.S + row;
+                        store_as(p.m_out, idx, p.out_dtype, m_true * p.scale);
+                        store_as(p.l_out, idx, p.out_dtype,
+                                 (m_true == -INFINITY) ? 0.f : l * ex2_approx((m_used - m_true) * c2));
+                    }
+                }
+            }
+            if (lead) tma_store_wait0();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort_flag && !skip) report_device_error(PMKL_DEVERR_TIMEOUT);
+}
+
+}  // namespace pp
+}  // namespace pmkl_b200

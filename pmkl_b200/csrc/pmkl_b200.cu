@@ -16,6 +16,7 @@
 #include <mutex>
 
 #include "attention_simt.cuh"
+#include "attention_pp.cuh"
 #include "attention_tc.cuh"
 #include "common.cuh"
 #include "pmkl_b200.h"
@@ -138,6 +139,65 @@ int launch_tc(const void *q, const void *k, const void *v, void *o, void *m, voi
     return launch_status();
 }
 
+int sm_count() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    return n;
+}
+
+// The persistent kernel re-splits its registers between warpgroups with
+// setmaxnreg; the split only fits when the kernel was built with exactly
+// pp::kLaunchRegs registers per thread.  Checked once per process.
+template <int D, bool BF16>
+bool pp_launchable() {
+    static int ok = -1;
+    if (ok < 0) {
+        cudaFuncAttributes attr;
+        ok = (cudaFuncGetAttributes(&attr, pp::attn_fwd_pp_kernel<D, BF16>) == cudaSuccess &&
+              attr.numRegs == pp::kLaunchRegs)
+                 ? 1
+                 : 0;
+        cudaGetLastError();
+    }
+    return ok == 1;
+}
+
+template <int D, bool BF16>
+int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int BH, int causal,
+              float scale, int dtype, int out_dtype, cudaStream_t stream) {
+    using C = pp::Cfg<D>;
+    static std::once_flag smem_once[kMaxDevices];
+    auto kernel = pp::attn_fwd_pp_kernel<D, BF16>;
+    if (!ensure_smem(kernel, C::kSmemBytes, smem_once)) return PMKL_ERR_LAUNCH;
+    CUtensorMap tq, tk, tv, to;
+    const bool o16 = out_dtype != PMKL_DTYPE_F32;
+    if (!make_tile_map(&tq, q, dtype, D, S, BH) || !make_tile_map(&tk, k, dtype, D, S, BH) ||
+        !make_tile_map(&tv, v, dtype, D, S, BH) || !make_tile_map(&to, o16 ? o : q, dtype, D, S, BH))
+        return PMKL_ERR_LAUNCH;
+    pp::Params p;
+    p.S = S;
+    p.BH = BH;
+    const int n_qt = (S + 127) / 128;
+    p.n_pairs = (n_qt + 1) / 2;
+    const long long units = static_cast<long long>(p.n_pairs) * BH;
+    if (units > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    p.n_units = static_cast<int>(units);
+    p.causal = causal;
+    p.out_dtype = out_dtype;
+    p.scale = scale;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.o_f32 = o;
+    p.m_out = m;
+    p.l_out = l;
+    const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
+    kernel<<<grid, pp::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+    return launch_status();
+}
+
 template <typename T, int DMAX>
 int launch_simt_t(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int D, int BH,
                   int causal, float scale, int out_dtype, cudaStream_t stream) {
@@ -177,7 +237,8 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
     if (out_dtype != dtype && out_dtype != PMKL_DTYPE_F32) return PMKL_ERR_INVALID_DTYPE;
-    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05)
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
         return PMKL_ERR_UNSUPPORTED;
     const long long BH = static_cast<long long>(batch) * heads;
     if (BH == 0 || seq == 0 || hidden == 0) return PMKL_OK;  // causal_attention.h:270
@@ -190,7 +251,22 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     const int causal = is_causal ? 1 : 0;
     const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype);
-    if (kernel == PMKL_ATTN_TCGEN05 && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if (kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05_SIMPLE && tc_ok) {
+        const int bh = static_cast<int>(BH);
+        const bool bf = dtype == PMKL_DTYPE_BF16;
+        const bool ready = hidden == 64 ? (bf ? pp_launchable<64, true>() : pp_launchable<64, false>())
+                                        : (bf ? pp_launchable<128, true>() : pp_launchable<128, false>());
+        if (ready) {
+            if (bf)
+                return hidden == 64
+                           ? launch_pp<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
+                           : launch_pp<128, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
+            return hidden == 64
+                       ? launch_pp<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
+                       : launch_pp<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
+        }
+    }
     if (kernel != PMKL_ATTN_SIMT && tc_ok) {
         const int bh = static_cast<int>(BH);
         if (dtype == PMKL_DTYPE_BF16)
