@@ -109,10 +109,36 @@ __device__ __forceinline__ Unit decode(const Params &p, int u) {
     return w;
 }
 
+// 2^x for x <= 0 on the FMA pipe, two lanes per instruction, to take load off
+// the MUFU unit (16 ex2 per clock per SM, which otherwise caps the softmax):
+//   x = n + f with n = round(x) (read from the low mantissa bits of
+//   x + 1.5*2^23) and f in [-1/2, 1/2];
+//   2^f by a degree-3 polynomial, a Chebyshev-node least-squares fit refined
+//   towards minimax (Lawson iterations), max relative error 7.5e-5 -- below
+//   the 2^-9 rounding that P gets anyway;
+//   2^n by adding n to the exponent field.
+// x is clamped to -125 so the result stays a normal number.
+__device__ __forceinline__ float2 exp2_poly(float2 x) {
+    using namespace ptx;
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -125.0f);
+    x.y = fmaxf(x.y, -125.0f);
+    const float2 r = add2(x, make_float2(kMagic, kMagic));
+    const float2 n = add2(r, make_float2(-kMagic, -kMagic));
+    const float2 f = fma2(n, make_float2(-1.0f, -1.0f), x);
+    float2 p = fma2(f, make_float2(0.0551716648f, 0.0551716648f), make_float2(0.2426111251f, 0.2426111251f));
+    p = fma2(p, f, make_float2(0.6932609677f, 0.6932609677f));
+    p = fma2(p, f, make_float2(0.9999280572f, 0.9999280572f));
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(r.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(r.y) << 23)));
+}
+
 // p = 2^(s * c2 - mref) for one 128-key score row, packed to 16-bit pairs and
 // stored into the P (hi) columns of the row's S buffer (and, with HILO, the
-// rounding remainder into the P (lo) columns).  Returns the fp32 row sum.
-template <bool BF16, bool HILO>
+// rounding remainder into the P (lo) columns).  In each 32-key chunk the first
+// NPOLY pairs go through exp2_poly, the rest through ex2.approx.  Returns the
+// fp32 row sum.
+template <bool BF16, bool HILO, int NPOLY>
 __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2, float mref, uint32_t sa) {
     using namespace ptx;
     float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
@@ -125,7 +151,7 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2,
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const float2 a = fma2(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), c22, nm2);
-            const float2 e = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+            const float2 e = (i < NPOLY) ? exp2_poly(a) : make_float2(ex2_approx(a.x), ex2_approx(a.y));
             rs2[i & 3] = add2(rs2[i & 3], e);
             ph[i] = pack2<BF16>(e.x, e.y);
             if constexpr (HILO) {
@@ -141,7 +167,13 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2,
     return rr.x + rr.y;
 }
 
-template <int D, bool BF16>
+// Pairs per 32-key chunk whose exp2 runs on the FMA pipe (0..16); the rest
+// use the MUFU unit.  A build-time knob, tuned on B200.
+#ifndef PMKL_PP_NPOLY
+#define PMKL_PP_NPOLY 0
+#endif
+
+template <int D, bool BF16, int NPOLY = PMKL_PP_NPOLY>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -256,28 +288,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             int qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
             int kvc = 0;
             bool ok = true;
-            auto issue_s = [&](int x, uint32_t k_addr) {
-                const uint32_t q_addr = smem_u32(sQ + x * TILE);
+            // Descriptors are built once; every operand slice is then the base
+            // descriptor plus a constant added to its 14-bit start-address field
+            // (addresses stay below 256 KB, so the field never carries over).
+            const uint64_t dq0 = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t dk0 = smem_desc_sw128(smem_u32(sRing), 16, 1024);         // K view of stage 0
+            const uint64_t dv0 = smem_desc_sw128(smem_u32(sRing), kBoxBytes, 1024);  // V view of stage 0
+            auto issue_s = [&](int x, int stage) {
+                const uint64_t a0 = dq0 + static_cast<uint64_t>(x * (TILE >> 4));
+                const uint64_t b0 = dk0 + static_cast<uint64_t>(stage * (TILE >> 4));
+                const uint32_t d = tmem + col_s(x);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                    mma_ss(tmem + col_s(x), smem_desc_sw128(q_addr + off, 16, 1024),
-                           smem_desc_sw128(k_addr + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+                    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4);
+                    mma_ss(d, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&s_full[x]);
             };
-            auto issue_pv = [&](int x, uint32_t v_addr, bool first, bool hilo) {
+            auto issue_pv = [&](int x, int stage, bool first, bool hilo) {
+                const uint64_t b0 = dv0 + static_cast<uint64_t>(stage * (TILE >> 4));
+                const uint32_t d = tmem + col_o(x);
+                const uint32_t a = tmem + col_s(x);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, kBoxBytes, 1024);
-                    mma_ts(tmem + col_o(x), tmem + col_s(x) + kPHi + kk * 8, b, kIdescO, (!first || kk > 0) ? 1u : 0u);
-                }
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(d, a + kPHi + kk * 8, b0 + static_cast<uint64_t>(kk * 128), kIdescO,
+                           (!first || kk > 0) ? 1u : 0u);
                 if (hilo) {
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, kBoxBytes, 1024);
-                        mma_ts(tmem + col_o(x), tmem + col_s(x) + kPLo + kk * 8, b, kIdescO, 1u);
-                    }
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts(d, a + kPLo + kk * 8, b0 + static_cast<uint64_t>(kk * 128), kIdescO, 1u);
                 }
             };
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
@@ -295,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 for (int x = 0; x < 2; ++x)
                     if (w.act[x]) {
-                        issue_s(x, smem_u32(sRing + sK * TILE));
+                        issue_s(x, sK);
                         if (w.n[x] == 1) mma_commit(&q_empty[x]);
                     }
                 mma_commit(&kv_empty[sK]);
@@ -304,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!(ok = mbar_wait(&kv_full[sV], (kvc / NS) & 1, abort_flag))) break;
                     ++kvc;
                     const bool has_next = j + 1 < w.n_max;
-                    int kvc_next = kvc;
+                    const int kvc_next = kvc;
                     if (has_next) {
                         sK = kvc % NS;
                         ++kvc;
@@ -316,14 +355,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ++pc[x];
                         if (j == 0 && oc[x] > 0 && !(ok = mbar_wait(&o_empty[x], (oc[x] - 1) & 1, abort_flag))) break;
                         tc_fence_after();
-                        issue_pv(x, smem_u32(sRing + sV * TILE), j == 0, w.hilo[x]);
+                        issue_pv(x, sV, j == 0, w.hilo[x]);
                         if (j + 1 < w.n[x]) {
                             if (!k_ready) {
                                 if (!(ok = mbar_wait(&kv_full[sK], (kvc_next / NS) & 1, abort_flag))) break;
                                 k_ready = true;
                                 tc_fence_after();
                             }
-                            issue_s(x, smem_u32(sRing + sK * TILE));
+                            issue_s(x, sK);
                             if (j + 2 == w.n[x]) mma_commit(&q_empty[x]);
                         } else {
                             mma_commit(&o_full[x]);
@@ -361,43 +400,61 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++sc;
                     tc_fence_after();
                     float s[128];
-                    {
-                        uint32_t *sr = reinterpret_cast<uint32_t *>(s);
-                        tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
-                        tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-                        tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-                        tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
-                        tmem_wait_ld();
-                    }
                     const int kbase = j * 128;
                     int lim = p.S - kbase;
                     if (p.causal) lim = min(lim, row - kbase + 1);
-                    if (lim < 128) {
-#pragma unroll
-                        for (int c = 0; c < 128; ++c)
-                            if (c >= lim) s[c] = -INFINITY;
-                    }
+                    const bool masked = __any_sync(0xffffffffu, lim < 128);
                     float mx8[8];
+                    {
+                        // Two halves: the max of the first overlaps the load of the second.
+                        uint32_t *sr = reinterpret_cast<uint32_t *>(s);
+                        tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                        tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                        tmem_wait_ld();
+                        tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+                        tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+                        if (masked) {
 #pragma unroll
-                    for (int t = 0; t < 8; ++t) mx8[t] = s[t];
+                            for (int c = 0; c < 64; ++c)
+                                if (c >= lim) s[c] = -INFINITY;
+                        }
 #pragma unroll
-                    for (int c = 8; c < 128; c += 8)
+                        for (int t = 0; t < 8; ++t) mx8[t] = s[t];
 #pragma unroll
-                        for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[c + t]);
+                        for (int c = 8; c < 64; c += 8)
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[c + t]);
+                        tmem_wait_ld();
+                        if (masked) {
+#pragma unroll
+                            for (int c = 64; c < 128; ++c)
+                                if (c >= lim) s[c] = -INFINITY;
+                        }
+#pragma unroll
+                        for (int c = 64; c < 128; c += 8)
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[c + t]);
+                    }
                     const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                            fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
                     m_true = fmaxf(m_true, mx);
                     const bool resc =
                         (m_used == -INFINITY) ? (m_true != -INFINITY) : ((m_true - m_used) * c2 > 8.0f);
+                    const bool any_resc = __any_sync(0xffffffffu, resc);
                     const float m_new = resc ? m_true : m_used;
-                    const float fac =
-                        resc ? ((m_used == -INFINITY) ? 0.f : ex2_approx((m_used - m_new) * c2)) : 1.f;
+                    float fac = 1.f;
+                    if (any_resc) fac = resc ? ((m_used == -INFINITY) ? 0.f : ex2_approx((m_used - m_new) * c2)) : 1.f;
                     const float mref = (m_new == -INFINITY) ? 0.f : m_new * c2;
-                    const float rsum = w.hilo[x] ? exp_pack_store<BF16, true>(s, c2, mref, sa)
-                                                 : exp_pack_store<BF16, false>(s, c2, mref, sa);
+                    float rsum;
+                    if (w.hilo[x])
+                        rsum = exp_pack_store<BF16, true, 0>(s, c2, mref, sa);
+                    else if (masked)
+                        rsum = exp_pack_store<BF16, false, 0>(s, c2, mref, sa);
+                    else
+                        rsum = exp_pack_store<BF16, false, NPOLY>(s, c2, mref, sa);
                     // O_X is idle here: S_X(j) was issued after PV_X(j-1), and
                     // its commit covers every earlier MMA.
-                    if (j > 0 && __any_sync(0xffffffffu, resc)) {
+                    if (j > 0 && any_resc) {
 #pragma unroll
                         for (int cc = 0; cc < D / 32; ++cc) {
                             uint32_t o[32];

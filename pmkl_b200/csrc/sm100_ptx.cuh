@@ -44,6 +44,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// Suspend hint for mbarrier.try_wait: the waiting thread is parked by the
+// hardware until the phase completes or this many nanoseconds pass, instead
+// of spinning on the issue port that the softmax warps need.
+constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -56,20 +61,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false when
 // the CTA-wide abort flag is raised or the wait exceeds kWaitTimeoutNs (in
 // which case this call raises the abort flag itself).  Single-thread form.
+// Each try_wait parks the thread for at most kSuspendHintNs, so the abort
+// flag and the deadline are checked at least that often.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 31u) == 0u) {
-            if (*abort_flag) return false;
-            if (globaltimer() - t0 > kWaitTimeoutNs) {
-                *abort_flag = 1;
-                return false;
-            }
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            return false;
         }
     }
 }
@@ -158,6 +175,50 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// Warp-collective forms of the single-thread issue instructions: the whole
+// (converged) warp executes them, one lane elected by elect.sync issues.  Run
+// by every lane, the surrounding loop keeps its addresses warp-uniform, which
+// lets the compiler hold them in uniform registers.
+__device__ __forceinline__ void mma_ss_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_elect(uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, e;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
 }
 
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
