@@ -76,10 +76,6 @@ __device__ __forceinline__ void unpack2(uint32_t u, float &lo, float &hi) {
     }
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -105,7 +101,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *bar_pfull = bar_sfree + 2;
     uint64_t *bar_odone = bar_pfull + 1;
     uint64_t *bar_final = bar_odone + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_final + 1);
+    uint64_t *bar_ostage = bar_final + 1;  // softmax warps -> store thread: O tile staged
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_ostage + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -133,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_pfull, 4);
         mbar_init(bar_odone, 1);
         mbar_init(bar_final, 1);
+        mbar_init(bar_ostage, 4);
         // Fast fail: once any CTA has abandoned a wait (the device error word
         // is set), later CTAs skip their work instead of each timing out.
         *abort_flag = (*reinterpret_cast<volatile unsigned int *>(&g_device_error) != 0u) ? 1 : 0;
@@ -378,8 +376,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 fence_proxy_async_smem();
-                named_bar_sync(1, 128);
-                if (threadIdx.x == 0) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_ostage);
+                // Bounded wait (not a named barrier): a warp that gave up earlier
+                // never arrives, and the store thread then gives up too.
+                if (threadIdx.x == 0 && mbar_wait(bar_ostage, 0, abort_flag)) {
 #pragma unroll
                     for (int b = 0; b < C::kBoxes; ++b) tma_store_3d(&tm_o, sQ + b * kBoxBytes, b * kBoxCols, qt * kBM, bh);
                     tma_store_commit();
