@@ -75,6 +75,7 @@ struct Params {
     int BH;
     int n_pairs;     // ceil(n_qt / 2)
     int n_units;     // n_pairs * BH
+    int group;       // (b, h) slices per scheduling group
     int causal;
     int out_dtype;
     float scale;
@@ -93,11 +94,21 @@ struct Unit {
     bool hilo[2];
 };
 
+// Work order: slices are taken in groups of p.group (b, h) slices whose K and
+// V together fit in L2, and inside a group the query-tile pairs go longest
+// first.  All pairs of a slice then run close together in time and re-read
+// that slice's K/V from L2 instead of HBM, while the longest-first order keeps
+// the CTAs' loads balanced.
 __device__ __forceinline__ Unit decode(const Params &p, int u) {
     Unit w;
     const int n_kv_all = (p.S + 127) / 128;
-    const int pair = p.causal ? (p.n_pairs - 1 - u / p.BH) : (u / p.BH);
-    w.bh = u % p.BH;
+    const int per_group = p.n_pairs * p.group;
+    const int g = u / per_group;
+    const int within = u - g * per_group;
+    const int g_slices = min(p.group, p.BH - g * p.group);
+    const int rank = within / g_slices;
+    const int pair = p.causal ? (p.n_pairs - 1 - rank) : rank;
+    w.bh = g * p.group + (within - rank * g_slices);
     w.row0 = pair * 256;
     for (int x = 0; x < 2; ++x) {
         const int r0 = w.row0 + 128 * x;

@@ -22,6 +22,12 @@
 #include "pmkl_b200.h"
 #include "softmax.cuh"
 
+// K+V bytes per scheduling group of the persistent attention kernel (tuned on
+// B200 at config 3: 24 MiB beat 48/96 MiB and no grouping).
+#ifndef PMKL_PP_GROUP_BYTES
+#define PMKL_PP_GROUP_BYTES (24LL << 20)
+#endif
+
 namespace pmkl_b200 {
 namespace {
 
@@ -186,6 +192,13 @@ int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, voi
     const long long units = static_cast<long long>(p.n_pairs) * BH;
     if (units > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
     p.n_units = static_cast<int>(units);
+    // Slices per scheduling group: K and V of a group stay within
+    // PMKL_PP_GROUP_BYTES of the 126 MB L2, at least one slice.
+    const long long kv_bytes = 2LL * S * D * 2;
+    long long grp = PMKL_PP_GROUP_BYTES / (kv_bytes > 0 ? kv_bytes : 1);
+    if (grp < 1) grp = 1;
+    if (grp > BH) grp = BH;
+    p.group = static_cast<int>(grp);
     p.causal = causal;
     p.out_dtype = out_dtype;
     p.scale = scale;
