@@ -53,7 +53,7 @@ WORKLOADS = {
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="attention", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="pmkl_b200", choices=["pmkl_b200", "reference"])
@@ -63,6 +63,9 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--kernel", type=int, default=0,
                     help="pmkl_attention_kernel value for the device-timed leg (0 = automatic choice)")
+    ap.add_argument("--shape", default=None,
+                    help="override the workload size for profiler captures: B,H,S,D for attention, "
+                         "ROWS,COLS for softmax (the bench line then describes that size)")
     return ap.parse_args()
 
 
@@ -350,6 +353,8 @@ def run_attention(args, wl, rank, world, local):
     def step():
         pmkl_b200.attention_fwd(q, k, v, o, m, l, causal, kernel=args.kernel, stream=stream)
 
+    kernel_name = pmkl_b200.attention_kernel_name(q, k, v, o, args.kernel)
+
     sampler = ClockSampler(world, (not args.no_clocks) and rank == 0)
     total_ms, per_ms = timed_loop(step, args.steps, args.warmup, world)
     clocks = sampler.stop()
@@ -414,7 +419,7 @@ def run_attention(args, wl, rank, world, local):
                      "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
                      "traffic": (traffic * ns if traffic is not None else None),
                      "algorithmic_bytes": 4 * q.numel() * q.element_size() + 2 * m.numel() * m.element_size(),
-                     "kernel": "attn_fwd_tc_kernel", "launch_ms_avg": launch_avg},
+                     "kernel": kernel_name, "launch_ms_avg": launch_avg},
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
@@ -493,6 +498,13 @@ def run_softmax(args, wl, rank, world, local):
 def main():
     args = parse_args()
     wl = WORKLOADS[args.workload]
+    if args.shape:
+        dims = [int(x) for x in args.shape.split(",")]
+        if args.workload == "softmax":
+            wl = (dims[0], dims[1]) + wl[2:7] + (f"warp softmax fp32 {dims[0]} x {dims[1]} (profiling size)",)
+        else:
+            wl = tuple(dims[:4]) + wl[4:7] + (f"causal self-attention {wl[4]} B{dims[0]} H{dims[1]} S{dims[2]} "
+                                              f"D{dims[3]} (profiling size)",)
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         line = run_reference_arm(args, wl, rank, int(os.environ.get("WORLD_SIZE", "1")))

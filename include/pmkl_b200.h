@@ -91,6 +91,13 @@ int pmkl_causal_attention_fwd_ex(const void *q, const void *k, const void *v, vo
                                  int batch, int heads, int seq, int hidden, int dtype, int out_dtype,
                                  int is_causal, float scale, int kernel, void *stream);
 
+/* The kernel pmkl_causal_attention_fwd_ex would run for these arguments:
+ * PMKL_ATTN_TCGEN05 (the persistent two-tile tensor-core kernel),
+ * PMKL_ATTN_TCGEN05_SIMPLE, PMKL_ATTN_SIMT, or a negative pmkl_status.  Needs
+ * a current sm_100 device.  No reference counterpart (diagnostic). */
+int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
+                                   int out_dtype, int kernel);
+
 /*
  * Row-wise softmax / log-softmax.
  *

@@ -71,6 +71,8 @@ def capi() -> ctypes.CDLL:
         L.pmkl_device_error.argtypes = [i32]
         L.pmkl_tc_selftest.restype = i32
         L.pmkl_tc_selftest.argtypes = [i32, vp, vp, vp, i32, i32, vp]
+        L.pmkl_attention_selected_kernel.restype = i32
+        L.pmkl_attention_selected_kernel.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32]
         _capi = L
     return _capi
 
@@ -99,6 +101,23 @@ def attention_fwd(q, k, v, o, m, l, is_causal: bool, scale: float = 0.0, kernel:
         int(kernel), _stream_ptr(stream))
     if rc != PMKL_OK:
         raise PmklError(rc, "pmkl_causal_attention_fwd")
+
+
+KERNEL_NAMES = {KERNEL_SIMT: "attn_fwd_simt_kernel", KERNEL_TCGEN05: "attn_fwd_pp_kernel",
+                3: "attn_fwd_tc_kernel"}
+
+
+def attention_selected_kernel(q, k, v, o, kernel: int = KERNEL_AUTO) -> int:
+    """The PMKL_ATTN_* kernel the library runs for these tensors."""
+    rc = capi().pmkl_attention_selected_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), q.shape[-1],
+                                               torch_dtype_code(q.dtype), torch_dtype_code(o.dtype), int(kernel))
+    if rc < 0:
+        raise PmklError(rc, "pmkl_attention_selected_kernel")
+    return rc
+
+
+def attention_kernel_name(q, k, v, o, kernel: int = KERNEL_AUTO) -> str:
+    return KERNEL_NAMES.get(attention_selected_kernel(q, k, v, o, kernel), "unknown")
 
 
 def warp_softmax_fwd(dst, src, elements: int, stride: int, rows: int, is_log: bool = False, stream=None) -> None:

@@ -244,6 +244,21 @@ bool tc_applies(const void *q, const void *k, const void *v, const void *o, int 
     return true;
 }
 
+// Which kernel runs: the persistent tensor-core kernel when it applies (and
+// its register split is available), the one-tile tensor-core kernel when
+// asked for or as the fallback, else the CUDA-core kernel.
+int select_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype, int out_dtype,
+                  int kernel) {
+    const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype);
+    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if (kernel == PMKL_ATTN_SIMT || !tc_ok) return PMKL_ATTN_SIMT;
+    if (kernel == PMKL_ATTN_TCGEN05_SIMPLE) return PMKL_ATTN_TCGEN05_SIMPLE;
+    const bool bf = dtype == PMKL_DTYPE_BF16;
+    const bool ready = hidden == 64 ? (bf ? pp_launchable<64, true>() : pp_launchable<64, false>())
+                                    : (bf ? pp_launchable<128, true>() : pp_launchable<128, false>());
+    return ready ? PMKL_ATTN_TCGEN05 : PMKL_ATTN_TCGEN05_SIMPLE;
+}
+
 int attention_impl(const void *q, const void *k, const void *v, void *o, void *m, void *l, int batch, int heads,
                    int seq, int hidden, int dtype, int out_dtype, int is_causal, float scale, int kernel,
                    void *stream_) {
@@ -263,24 +278,17 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     const float sc = (scale > 0.f) ? scale : 1.0f / sqrtf(static_cast<float>(hidden));
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     const int causal = is_causal ? 1 : 0;
-    const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype);
-    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
-    if (kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05_SIMPLE && tc_ok) {
+    const int chosen = select_kernel(q, k, v, o, hidden, dtype, out_dtype, kernel);
+    if (chosen < 0) return chosen;
+    if (chosen == PMKL_ATTN_TCGEN05) {
         const int bh = static_cast<int>(BH);
-        const bool bf = dtype == PMKL_DTYPE_BF16;
-        const bool ready = hidden == 64 ? (bf ? pp_launchable<64, true>() : pp_launchable<64, false>())
-                                        : (bf ? pp_launchable<128, true>() : pp_launchable<128, false>());
-        if (ready) {
-            if (bf)
-                return hidden == 64
-                           ? launch_pp<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
-                           : launch_pp<128, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
-            return hidden == 64
-                       ? launch_pp<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
-                       : launch_pp<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
-        }
+        if (dtype == PMKL_DTYPE_BF16)
+            return hidden == 64 ? launch_pp<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
+                                : launch_pp<128, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
+        return hidden == 64 ? launch_pp<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
+                            : launch_pp<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
     }
-    if (kernel != PMKL_ATTN_SIMT && tc_ok) {
+    if (chosen == PMKL_ATTN_TCGEN05_SIMPLE) {
         const int bh = static_cast<int>(BH);
         if (dtype == PMKL_DTYPE_BF16)
             return hidden == 64 ? launch_tc<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
@@ -374,6 +382,17 @@ int pmkl_causal_attention_fwd_ex(const void *q, const void *k, const void *v, vo
                                  int kernel, void *stream) {
     return attention_impl(q, k, v, o, m, l, batch, heads, seq, hidden, dtype, out_dtype, is_causal, scale, kernel,
                           stream);
+}
+
+int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
+                                   int out_dtype, int kernel) {
+    if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
+        return PMKL_ERR_UNSUPPORTED;
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    return select_kernel(q, k, v, o, hidden, dtype, out_dtype, kernel);
 }
 
 int pmkl_warp_softmax_fwd(void *dst, const void *src, int elements, int stride, int rows, int in_dtype,

@@ -276,6 +276,19 @@ def test_simt_and_tc_agree():
     assert (a[1] - b[1]).abs().max().item() < 1e-4
 
 
+@pytest.mark.parametrize("dtype", LP)
+@pytest.mark.parametrize("D", [64, 128])
+def test_native_tensor_core_kernel_is_selected(D, dtype):
+    """16-bit inputs with head size 64/128 run the persistent tcgen05 kernel
+    (not a fallback); fp32 and other head sizes run the CUDA-core kernel."""
+    q = torch.zeros(1, 1, 256, D, dtype=dtype, device="cuda")
+    assert pmkl_b200.attention_selected_kernel(q, q, q, q) == TC
+    q32 = q.float()
+    assert pmkl_b200.attention_selected_kernel(q32, q32, q32, q32) == SIMT
+    q96 = torch.zeros(1, 1, 256, 96, dtype=dtype, device="cuda")
+    assert pmkl_b200.attention_selected_kernel(q96, q96, q96, q96) == SIMT
+
+
 # ------------------------------------------------------------------ errors on the device path
 def test_tc_rejects_unsupported_head_size():
     q = torch.zeros(1, 1, 16, 96, dtype=torch.bfloat16, device="cuda")
