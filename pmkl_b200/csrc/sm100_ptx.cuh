@@ -104,8 +104,8 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 3-D tiled load (no multicast): box at coordinates (x, y, z) into smem,
-// completion signalled on `bar` as transaction bytes.
+// 3-D tiled load into this CTA's own shared memory: box at coordinates
+// (x, y, z), completion signalled on `bar` as transaction bytes.
 __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int x, int y,
                                             int z) {
     asm volatile(
