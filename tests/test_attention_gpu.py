@@ -154,6 +154,30 @@ def test_peaked_scores_bf16_p_bound():
     assert_lp_close(np32(m), rm, torch.bfloat16, "m")
 
 
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("dtype", LP)
+def test_row_max_jumps_after_first_key_tile(causal, D, dtype):
+    """Keys of the later key tiles are scaled up (x6 for keys 128..255, x12
+    beyond), so most rows' maxima jump by far more than 2^8 after the first key
+    tile: the kernel's exp reference point must move and the tile be redone.
+    Same P-rounding bound as the peaked-score test."""
+    q, k, v = seeded_qkv(1, 3, 640, D, dtype, seed=17)
+    k = k.clone()
+    k[:, :, 128:256] *= 6
+    k[:, :, 256:] *= 12
+    o, m, l = attention_capi(q, k, v, causal, kernel=TC)
+    ro, rm, rl = oracle.attention_fwd(np32(q), np32(k), np32(v), causal)
+    got = np32(o).astype(np.float64)
+    vmax = float(np.abs(np32(v)).max())
+    mant = 7 if dtype == torch.bfloat16 else 10
+    half_ulp = 0.5 * (2.0 ** (np.floor(np.log2(np.maximum(np.abs(ro), 1e-30))) - mant))
+    assert (np.abs(got - ro) <= 2.0 ** -8 * vmax + half_ulp).all()
+    assert_lp_close(np32(m), rm, dtype, "m")
+    rel = np.abs(np32(l) - rl) / np.maximum(rl, 1.0)
+    assert rel.max() <= 2e-3 + 0.5 * 2.0 ** -mant
+
+
 # ------------------------------------------------------------------ benchmark configurations
 def test_config1_fp32():
     """fp32 B2 H4 S128 D64 causal (also a golden fixture)."""
