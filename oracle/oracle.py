@@ -48,6 +48,10 @@ def lib():
         L.pmkl_oracle_attention_fwd_f32.argtypes = [vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, ctypes.c_float]
         L.pmkl_oracle_attention_rows_f32.restype = i32
         L.pmkl_oracle_attention_rows_f32.argtypes = [vp, vp, vp, i32, i32, i32, ctypes.c_float, vp, vp, i64, vp, vp, vp]
+        L.pmkl_oracle_attention_bwd_exact_f32.restype = None
+        L.pmkl_oracle_attention_bwd_exact_f32.argtypes = [vp] * 9 + [i64, i32, i32, i32]
+        L.pmkl_oracle_attention_bwd_f32.restype = i32
+        L.pmkl_oracle_attention_bwd_f32.argtypes = [vp] * 9 + [i64, i32, i32, i32, ctypes.c_float]
         for name in ("pmkl_oracle_softmax_fwd_f32", "pmkl_oracle_log_softmax_fwd_f32"):
             fn = getattr(L, name)
             fn.restype = None
@@ -107,6 +111,30 @@ def attention_rows(q, k, v, causal: bool, slices, rows, scale=None):
     if rc != 0:
         raise MemoryError("oracle scratch allocation failed")
     return o, m, l
+
+
+def attention_bwd(dout, q, k, v, m, l, causal: bool, scale=None, exact: bool = False):
+    """Gradients of fused_self_attention (fused_self_attention.cpp:66-135):
+    (dq, dk, dv) in fp32 for dout, q, k, v [B, H, S, D] and the forward's m, l
+    [B, H, S], all upcast to fp32.  ``exact`` runs the reference's O(S^3 D) loop
+    as written (fp32, bit-identical to it; default scale only); otherwise the
+    O(S^2 D) double-accumulation form."""
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (dout, q, k, v, m, l)]
+    dout, q, k, v, m, l = arrs
+    B, H, S, D = q.shape
+    assert k.shape == q.shape and v.shape == q.shape and dout.shape == q.shape
+    assert m.shape == (B, H, S) and l.shape == (B, H, S)
+    dq, dk, dv = np.empty_like(q), np.empty_like(q), np.empty_like(q)
+    args = [_ptr(a) for a in (dout, q, k, v, m, l, dq, dk, dv)]
+    if exact:
+        assert scale is None or np.float32(scale) == default_scale(D)
+        lib().pmkl_oracle_attention_bwd_exact_f32(*args, B * H, S, D, int(bool(causal)))
+    else:
+        scale = default_scale(D) if scale is None else np.float32(scale)
+        rc = lib().pmkl_oracle_attention_bwd_f32(*args, B * H, S, D, int(bool(causal)), float(scale))
+        if rc != 0:
+            raise MemoryError("oracle scratch allocation failed")
+    return dq, dk, dv
 
 
 def softmax_fwd(x, elements: int | None = None, stride: int | None = None, rows: int | None = None,

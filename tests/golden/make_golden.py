@@ -8,7 +8,8 @@ Each ``.npz`` holds the inputs and the reference's outputs; the CPU tests
 replay the inputs through the oracle and through the CUDA path.
 
 Attention fixtures call ``fused_self_attention_fw`` of the reference extension
-(``pmkl_pytorch_ext/fused_self_attention.cpp:139-173``).  Softmax fixtures call
+(``pmkl_pytorch_ext/fused_self_attention.cpp:139-173``); backward fixtures
+(``attn_bwd_*``) also call ``fused_self_attention_bw`` (``:175-215``).  Softmax fixtures call
 ``host_softmax_forward<float,float,float>`` (``test/test_softmax.cpp:10-28``).
 Half/bfloat16 tensors are stored as their raw 16-bit patterns (numpy has no
 bfloat16).
@@ -47,6 +48,16 @@ ATTN_CASES = [
     ("attn_s64_d128_bf16_causal_std05", 1, 2, 64, 128, True, torch.bfloat16, 11, 0.5),
 ]
 
+# Backward fixtures: (name, B, H, S, D, causal, torch dtype, seed).  m, l come
+# from the reference's forward on the same inputs, dout is N(0, 1).
+BWD_CASES = [
+    ("attn_bwd_s64_d64_f32_causal", 1, 2, 64, 64, True, torch.float32, 30),
+    ("attn_bwd_s77_d128_f32_full", 1, 1, 77, 128, False, torch.float32, 31),
+    ("attn_bwd_s130_d64_f32_causal", 1, 1, 130, 64, True, torch.float32, 32),
+    ("attn_bwd_s5_d32_f32_causal", 2, 1, 5, 32, True, torch.float32, 33),
+    ("attn_bwd_s48_d64_bf16_causal", 1, 2, 48, 64, True, torch.bfloat16, 34),
+]
+
 # (name, rows, elements, stride, seed, std)
 SOFTMAX_CASES = [
     ("softmax_12x1024", 12, 1024, 1024, 20, 2.0),  # test_softmax.cpp:33-34 shape, N(0,4) values
@@ -75,6 +86,23 @@ def make_attention(ext) -> None:
         print("wrote", name)
 
 
+def make_attention_bwd(ext) -> None:
+    """``fused_self_attention_bw`` (fused_self_attention.cpp:175-215) on the
+    forward's own m, l."""
+    for name, B, H, S, D, causal, dtype, seed in BWD_CASES:
+        g = torch.Generator().manual_seed(seed)
+        q, k, v, do = [torch.randn(B, H, S, D, generator=g).to(dtype) for _ in range(4)]
+        o, m, l = ext.fused_self_attention_fw(q, k, v, causal)
+        dq, dk, dv = ext.fused_self_attention_bw(do, q, k, v, m, l, causal)
+        np.savez_compressed(
+            HERE / f"{name}.npz",
+            q=_raw(q), k=_raw(k), v=_raw(v), do=_raw(do), m=_raw(m), l=_raw(l),
+            dq=_raw(dq), dk=_raw(dk), dv=_raw(dv),
+            causal=np.array(causal), dtype=np.array(str(dtype).replace("torch.", "")),
+        )
+        print("wrote", name)
+
+
 def make_softmax(fn) -> None:
     for name, rows, elements, stride, seed, std in SOFTMAX_CASES:
         g = torch.Generator().manual_seed(seed)
@@ -91,6 +119,7 @@ def main() -> None:
         raise SystemExit("reference tree not found; set PMKL_REFERENCE_DIR")
     torch.set_num_threads(1)
     make_attention(build_ref.load_ref_ext())
+    make_attention_bwd(build_ref.load_ref_ext())
     make_softmax(build_ref.load_ref_softmax())
 
 
