@@ -47,7 +47,10 @@ WORKLOADS = {
     "attention-cfg2": (8, 16, 1024, 64, "float16", 1.0, True, "BASELINE config 2: causal self-attention fp16 B8 H16 S1024 D64"),
     "attention-cfg4": (1, 32, 32768, 128, "bfloat16", 0.5, True, "BASELINE config 4: causal self-attention bf16 B1 H32 S32768 D128"),
     "softmax": (65536, 1024, None, None, "float32", 2.0, None, "BASELINE config 5: warp softmax fp32 65536 x 1024"),
+    "attention-bwd": (16, 32, 4096, 128, "bfloat16", 1.0, True,
+                      "backward of BASELINE config 3: fused_self_attention_bw bf16 B16 H32 S4096 D128 causal"),
 }
+BWD_METRIC = "causal attention backward TFLOP/s (whole box)"
 
 
 def parse_args():
@@ -72,6 +75,12 @@ def parse_args():
 def attn_flops_per_slice(S: int, D: int, causal: bool) -> float:
     pairs = S * (S + 1) / 2 if causal else S * S
     return 4.0 * D * pairs
+
+
+def attn_bwd_flops_per_slice(S: int, D: int, causal: bool) -> float:
+    """The five contractions of the backward (S, dP, dV, dK, dQ) over the
+    unmasked pairs: 2.5 x the forward's."""
+    return 2.5 * attn_flops_per_slice(S, D, causal)
 
 
 def shard(n_units: int, world: int, rank: int) -> tuple[int, int]:
@@ -239,6 +248,32 @@ def _ref_attention_worker(args):
     return time.perf_counter() - t0
 
 
+def _ref_attention_bwd_worker(args):
+    """Runs the reference's CPU backward (fused_self_attention_bw of its torch
+    extension, O(S^3 D)) on one seeded r-row problem; returns seconds."""
+    r, D, dtype_name, std, causal, seed = args
+    import torch
+
+    torch.set_num_threads(1)
+    from oracle import build_ref
+
+    ext = build_ref.load_ref_ext()
+    dt = getattr(torch, dtype_name)
+    g = torch.Generator().manual_seed(seed)
+    q, k, v, do = [(torch.randn(1, 1, r, D, generator=g) * std).to(dt) for _ in range(4)]
+    _, m, l = ext.fused_self_attention_fw(q, k, v, causal)
+    t0 = time.perf_counter()
+    ext.fused_self_attention_bw(do, q, k, v, m, l, causal)
+    return time.perf_counter() - t0
+
+
+def pick_bwd_rows(D: int, dtype_name: str, causal: bool, budget_s: float) -> int:
+    """Largest r whose single-core reference backward (time ~ r^3) fits budget_s."""
+    t = _ref_attention_bwd_worker((32, D, dtype_name, 1.0, causal, 0))
+    r = int(32 * (budget_s / max(t, 1e-6)) ** (1.0 / 3.0))
+    return max(16, min(512, r))
+
+
 def _ref_softmax_worker(args):
     rows, el, seed = args
     import numpy as np
@@ -300,14 +335,22 @@ def run_reference_arm(args, wl, rank, world):
         unit_per_step = cores * rows * el * 8.0 / 1e9  # GB moved per step (read + write fp32)
         unit, metric = "GB/s", "warp softmax GB/s (whole box)"
         sample = f"reference host_softmax_forward (CPU fp32), {rows} rows x {el} per core per step"
-    else:
+    elif args.workload != "attention-bwd":
         r = pick_prefix_rows(S, D, dtype_name, causal, budget)
         work = [(r, D, dtype_name, std, causal, 100 + i) for i in range(cores)]
         unit_per_step = cores * attn_flops_per_slice(r, D, causal) / 1e12
         unit, metric = "TFLOP/s", ATTN_METRIC
         sample = (f"reference fused_self_attention_fw (CPU, {dtype_name}): per step each of {cores} worker "
                   f"processes runs a causal prefix of {r} of {S} rows of one (b,h) slice, D={D}")
-    fn = _ref_softmax_worker if args.workload == "softmax" else _ref_attention_worker
+    elif args.workload == "attention-bwd":
+        r = pick_bwd_rows(D, dtype_name, causal, budget)
+        work = [(r, D, dtype_name, std, causal, 100 + i) for i in range(cores)]
+        unit_per_step = cores * attn_bwd_flops_per_slice(r, D, causal) / 1e12
+        unit, metric = "TFLOP/s", BWD_METRIC
+        sample = (f"reference fused_self_attention_bw (CPU, {dtype_name}, O(S^3 D)): per step each of {cores} "
+                  f"worker processes runs the backward of one {r}-row causal (b,h) problem, D={D}")
+    fn = {"softmax": _ref_softmax_worker, "attention-bwd": _ref_attention_bwd_worker}.get(args.workload,
+                                                                                          _ref_attention_worker)
     times = []
     with ctx.Pool(cores) as pool:
         for i in range(total_steps):
@@ -426,6 +469,104 @@ def run_attention(args, wl, rank, world, local):
     return line
 
 
+def run_attention_bwd(args, wl, rank, world, local):
+    """One step = pmkl_causal_attention_bwd over the rank's (b, h) shard: the
+    forward with fp32 outputs (delta needs O, which the reference's backward
+    does not take), the row-statistics kernel, the dQ kernel and the dK/dV
+    kernel.  m, l come from one forward before the timed region, in the input
+    dtype as the reference returns them."""
+    import torch
+
+    import pmkl_b200
+    import pmkl_pytorch_ext
+
+    B, H, S, D, dtype_name, std, causal, desc = wl
+    dt = getattr(torch, dtype_name)
+    n_slices = B * H
+    lo, hi = shard(n_slices, world, rank)
+    ns = hi - lo
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    q, k, v, do = [(torch.randn(ns, 1, S, D, generator=g, device=dev) * std).to(dt) for _ in range(4)]
+    o = torch.empty_like(q)
+    m = torch.empty(ns, 1, S, dtype=dt, device=dev)
+    l = torch.empty_like(m)
+    pmkl_b200.attention_fwd(q, k, v, o, m, l, causal)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws = torch.empty(pmkl_b200.attention_bwd_workspace_size(ns, 1, S, D, dt), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        pmkl_b200.attention_bwd(do, q, k, v, m, l, dq, dk, dv, causal, kernel=args.kernel, workspace=ws,
+                                stream=stream)
+
+    sampler = ClockSampler(world, (not args.no_clocks) and rank == 0)
+    total_ms, per_ms = timed_loop(step, args.steps, args.warmup, world)
+    clocks = sampler.stop()
+    flops_rank = ns * attn_bwd_flops_per_slice(S, D, causal)
+    flops_all = n_slices * attn_bwd_flops_per_slice(S, D, causal)
+    t_max = max_over_ranks(total_ms, world)
+    value = flops_all * args.steps / (t_max / 1e3) / 1e12
+    launch_avg = statistics.mean(per_ms)
+    achieved = -max_over_ranks(-(flops_rank / (launch_avg / 1e3) / 1e12), world)
+    peaks = measured_peaks()
+
+    # End to end through the reference-facing binding: H2D of dout, q, k, v, m,
+    # l from pinned memory, fused_self_attention_bw, D2H of dq, dk, dv.
+    hosts = [t.cpu().pin_memory() for t in (do, q, k, v, m, l)]
+    devs = [torch.empty_like(t) for t in (do, q, k, v, m, l)]
+    outs_h = [torch.empty(q.shape, dtype=dt).pin_memory() for _ in range(3)]
+
+    def e2e_step():
+        for d_, h_ in zip(devs, hosts):
+            d_.copy_(h_, non_blocking=True)
+        grads = pmkl_pytorch_ext.fused_self_attention_bw(*devs, causal)
+        for h_, g_ in zip(outs_h, grads):
+            h_.copy_(g_, non_blocking=True)
+
+    e2e_steps = max(1, min(args.e2e_steps, args.steps))
+    e2e_ms, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
+    e2e_value = flops_all * e2e_steps / (max_over_ranks(e2e_ms, world) / 1e3) / 1e12
+    h2d = sum(t.numel() * t.element_size() for t in hosts)
+    d2h = sum(t.numel() * t.element_size() for t in outs_h)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            r = pick_bwd_rows(D, dtype_name, causal, 15.0)
+            tt = _ref_attention_bwd_worker((r, D, dtype_name, std, causal, 7))
+            cpu = {"value": attn_bwd_flops_per_slice(r, D, causal) / tt / 1e12, "unit": "TFLOP/s", "cores": 1,
+                   "kind": "reference",
+                   "sample": f"reference fused_self_attention_bw (CPU, {dtype_name}, O(S^3 D) as written) on one "
+                             f"{r}-row causal (b,h) problem, D={D}, {tt:.1f} s on 1 core"}
+        except FileNotFoundError as e:
+            cpu = {"value": None, "unit": "TFLOP/s", "cores": 1, "kind": "reference", "sample": f"unavailable: {e}"}
+
+    return {
+        "metric": BWD_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": dtype_name, "data": f"synthetic, seeded N(0, {std}^2) generated on device",
+        "config": {"workload": desc, "B": B, "H": H, "S": S, "D": D, "causal": causal,
+                   "parallelism": f"(batch, head) shards over {world} GPU(s), no inter-GPU traffic",
+                   "slices_per_gpu": ns, "flop_convention": "10*D*S(S+1)/2 per (b,h) slice (5 contractions)",
+                   "l2": "inputs (4 x %.0f MiB per GPU) exceed the 126 MB L2; no flush" % (q.numel() * q.element_size() / 2**20)},
+        "per_gpu_tflops": value / world,
+        "frac_of_peak": value / world / peaks["bf16_tflops"],
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "pmkl_pytorch_ext.fused_self_attention_bw", "steps": e2e_steps},
+        "gpu_launches": 4 * args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"],
+                     "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
+                     "traffic": None,
+                     "kernel": "one backward call: attn_fwd_pp_kernel (fp32 out) + bwd_rowstat_kernel + "
+                               "attn_bwd_dq_kernel + attn_bwd_dkv_kernel",
+                     "launch_ms_avg": launch_avg},
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+
+
 def run_softmax(args, wl, rank, world, local):
     import torch
 
@@ -515,6 +656,8 @@ def main():
     try:
         if args.workload == "softmax":
             line = run_softmax(args, wl, rank, world, local)
+        elif args.workload == "attention-bwd":
+            line = run_attention_bwd(args, wl, rank, world, local)
         else:
             line = run_attention(args, wl, rank, world, local)
         if rank == 0:

@@ -44,6 +44,7 @@ typedef enum pmkl_status {
     PMKL_ERR_NO_DEVICE = -6,       /* no CUDA device, or not an sm_100 device */
     PMKL_ERR_LAUNCH = -7,          /* the CUDA runtime rejected the launch */
     PMKL_ERR_DEVICE_TIMEOUT = -8,  /* a kernel gave up on a bounded wait (see pmkl_device_error) */
+    PMKL_ERR_WORKSPACE = -9,       /* workspace smaller than the call needs */
 } pmkl_status;
 
 /* Kernel selection for pmkl_causal_attention_fwd_ex. */
@@ -97,6 +98,51 @@ int pmkl_causal_attention_fwd_ex(const void *q, const void *k, const void *v, vo
  * a current sm_100 device.  No reference counterpart (diagnostic). */
 int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
                                    int out_dtype, int kernel);
+
+/*
+ * Fused (causal) self-attention backward.
+ *
+ * Replaces fused_self_attention_bw (pmkl_pytorch_ext/fused_self_attention.cpp:
+ * 175-215), whose math is pmkl_cpu::host_self_attention_backward (:66-135);
+ * the reference has no GPU backward.  Gradients of o with respect to q, k, v
+ * given dout = dL/do and the forward's row statistics m, l as the caller
+ * passes them (used as given: p = exp(scale q.k - m) / l, as :91 does):
+ *   dv = P^T dout,  dS = P * (dout v^T - delta),  delta_i = sum_j P_ij (dout_i . v_j),
+ *   dq = scale dS k,  dk = scale dS^T q.
+ *
+ *   dout, q, k, v, dq, dk, dv : [batch, heads, seq, hidden], contiguous, `dtype`.
+ *   m, l                      : [batch, heads, seq], `dtype` (the forward's
+ *                               outputs, which the reference returns in v's dtype).
+ *   scale                     : as in the forward (<= 0: 1/sqrt(hidden), the
+ *                               reference's fixed value, :90).
+ *   workspace                 : device scratch of at least
+ *                               pmkl_causal_attention_bwd_workspace_size(...)
+ *                               bytes, 256-byte aligned; its contents on entry
+ *                               do not matter.  Not used after the call's work
+ *                               completes on `stream`.
+ *
+ * dq, dk, dv are written, not accumulated (the reference zero-fills them first,
+ * :186-188, so the results agree).  Accumulation is fp32; 16-bit outputs are
+ * rounded once.  fp16/bf16 with hidden 64 or 128 and 16-byte aligned pointers
+ * run on the tensor cores; everything else on the CUDA-core path.
+ */
+int pmkl_causal_attention_bwd(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                              const void *l, void *dq, void *dk, void *dv, int batch, int heads, int seq,
+                              int hidden, int dtype, int is_causal, float scale, void *workspace,
+                              size_t workspace_bytes, void *stream);
+
+/* As pmkl_causal_attention_bwd with an explicit kernel choice: PMKL_ATTN_AUTO,
+ * PMKL_ATTN_SIMT or PMKL_ATTN_TCGEN05 (PMKL_ERR_UNSUPPORTED when the tensor-core
+ * path does not cover the arguments). */
+int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                                 const void *l, void *dq, void *dk, void *dv, int batch, int heads, int seq,
+                                 int hidden, int dtype, int is_causal, float scale, void *workspace,
+                                 size_t workspace_bytes, int kernel, void *stream);
+
+/* Workspace bytes pmkl_causal_attention_bwd needs for these sizes (enough for
+ * either path; 0 for an empty problem).  No reference counterpart: the
+ * reference's CPU backward needs no scratch. */
+size_t pmkl_causal_attention_bwd_workspace_size(int batch, int heads, int seq, int hidden, int dtype);
 
 /*
  * Row-wise softmax / log-softmax.

@@ -59,6 +59,12 @@ def capi() -> ctypes.CDLL:
         L.pmkl_causal_attention_fwd.argtypes = [vp] * 6 + [i32] * 7 + [f32, vp]
         L.pmkl_causal_attention_fwd_ex.restype = i32
         L.pmkl_causal_attention_fwd_ex.argtypes = [vp] * 6 + [i32] * 7 + [f32, i32, vp]
+        L.pmkl_causal_attention_bwd.restype = i32
+        L.pmkl_causal_attention_bwd.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp, ctypes.c_size_t, vp]
+        L.pmkl_causal_attention_bwd_ex.restype = i32
+        L.pmkl_causal_attention_bwd_ex.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp, ctypes.c_size_t, i32, vp]
+        L.pmkl_causal_attention_bwd_workspace_size.restype = ctypes.c_size_t
+        L.pmkl_causal_attention_bwd_workspace_size.argtypes = [i32] * 5
         L.pmkl_warp_softmax_fwd.restype = i32
         L.pmkl_warp_softmax_fwd.argtypes = [vp, vp] + [i32] * 6 + [vp]
         L.pmkl_status_string.restype = ctypes.c_char_p
@@ -101,6 +107,30 @@ def attention_fwd(q, k, v, o, m, l, is_causal: bool, scale: float = 0.0, kernel:
         int(kernel), _stream_ptr(stream))
     if rc != PMKL_OK:
         raise PmklError(rc, "pmkl_causal_attention_fwd")
+
+
+def attention_bwd_workspace_size(B: int, H: int, S: int, D: int, dtype) -> int:
+    return int(capi().pmkl_causal_attention_bwd_workspace_size(B, H, S, D, torch_dtype_code(dtype)))
+
+
+def attention_bwd(dout, q, k, v, m, l, dq, dk, dv, is_causal: bool, scale: float = 0.0, kernel: int = KERNEL_AUTO,
+                  workspace=None, stream=None) -> None:
+    """Calls pmkl_causal_attention_bwd_ex on caller-allocated torch CUDA tensors
+    (dout, q, k, v, dq, dk, dv: [B, H, S, D]; m, l: [B, H, S], all one dtype).
+    ``workspace`` is a uint8 CUDA tensor of at least attention_bwd_workspace_size
+    bytes; one is allocated when it is None.  Raises PmklError."""
+    import torch
+
+    B, H, S, D = q.shape
+    if workspace is None:
+        workspace = torch.empty(max(attention_bwd_workspace_size(B, H, S, D, q.dtype), 1), dtype=torch.uint8,
+                                device=q.device)
+    rc = capi().pmkl_causal_attention_bwd_ex(
+        dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), m.data_ptr(), l.data_ptr(), dq.data_ptr(),
+        dk.data_ptr(), dv.data_ptr(), B, H, S, D, torch_dtype_code(q.dtype), int(bool(is_causal)), float(scale),
+        workspace.data_ptr(), workspace.numel(), int(kernel), _stream_ptr(stream))
+    if rc != PMKL_OK:
+        raise PmklError(rc, "pmkl_causal_attention_bwd")
 
 
 KERNEL_NAMES = {KERNEL_SIMT: "attn_fwd_simt_kernel", KERNEL_TCGEN05: "attn_fwd_pp_kernel",

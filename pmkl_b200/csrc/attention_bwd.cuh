@@ -1,0 +1,607 @@
+// attention_bwd.cuh -- tensor-core (tcgen05) backward of the fused causal
+// self-attention for sm_100a, fp16/bf16 inputs, head size 64 or 128.
+//
+// Gradients of what fused_self_attention_bw computes
+// (pmkl_pytorch_ext/fused_self_attention.cpp:66-135), given dO, Q, K, V and
+// the forward's row statistics m~, l~ as the caller passes them:
+//   p_nj  = exp(s_nj - m~_n) / l~_n,   s = scale Q K^T (masked: p = 0)
+//   dP_nj = dO_n . V_j,   delta_n = sum_j p_nj dP_nj
+//   dS_nj = p_nj (dP_nj - delta_n)
+//   dQ = scale dS K,   dK = scale dS^T Q,   dV = P^T dO
+// (the reference's innermost loop, :99-121, sums exactly scale p_nm (dP_nm -
+// delta_n) for each (n, m)).  Three launches, no atomics, deterministic:
+//   1. bwd_rowstat_kernel: per query row, b_n = m~_n log2 e + log2 l~_n (so
+//      that p = 2^(s c2 - b_n) with c2 = scale log2 e) and delta_n.  delta
+//      comes from this library's own forward (O, m, l in fp32) through
+//        sum_j p_nj dP_nj = exp(m_n - m~_n) (l_n / l~_n) (dO_n . O_n),
+//      exact algebra, because the reference backward takes no O.
+//   2. attn_bwd_dq_kernel: one CTA per (slice, 128-row query tile); per key
+//      tile S = Q K^T and dP = dO V^T into tensor memory, dS (16-bit) back
+//      into tensor memory, dQ += dS K.
+//   3. attn_bwd_dkv_kernel: one CTA per (slice, 128-row key tile); per query
+//      tile S^T = K Q^T and dP^T = V dO^T, P^T and dS^T (16-bit) back into
+//      tensor memory, dV += P^T dO and dK += dS^T Q.
+// Both gradient kernels: warps 0-3 are the elementwise warps (one thread per
+// tensor-memory lane = tile row), warp 4 issues TMA loads, warp 5 (one
+// thread) issues tcgen05.mma.  Every wait is bounded (sm100_ptx.cuh).
+#pragma once
+
+#include "attention_tc.cuh"
+
+namespace pmkl_b200 {
+namespace bwd {
+
+using tc::kBoxBytes;
+using tc::kBoxCols;
+
+constexpr int kThreads = 192;
+constexpr int kWarpTma = 4;
+constexpr int kWarpMma = 5;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;      // S or S^T (fp32); the 16-bit P / dS packed into its first 64 columns
+constexpr uint32_t kColDP = 128;   // dP or dP^T (fp32); the 16-bit dS^T packed into its first 64 columns
+constexpr uint32_t kColAcc = 256;  // dQ; or dV at kColAcc and dK at kColAcc + D
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kStatBytes = 128 * 8;  // (b, delta) of one 128-row query tile
+
+struct Params {
+    int S;
+    int S_pad;   // row pitch of the row statistics (a multiple of 128)
+    int BH;
+    int n_qt;    // 128-row tiles per slice
+    int causal;
+    float scale;
+    float scale_log2;
+    const float2 *rowstat;  // [BH][S_pad]: (b_n, delta_n)
+};
+
+template <typename T>
+__device__ __forceinline__ float load_f(const void *base, size_t idx) {
+    return Elem<T>::to_float(static_cast<const T *>(base)[idx]);
+}
+template <>
+__device__ __forceinline__ float load_f<float>(const void *base, size_t idx) {
+    return static_cast<const float *>(base)[idx];
+}
+
+// One warp per row of the padded [BH][S_pad] grid.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    bwd_rowstat_kernel(const T *__restrict__ dout, const float *__restrict__ o32, const float *__restrict__ m32,
+                       const float *__restrict__ l32, const void *__restrict__ m_in, const void *__restrict__ l_in,
+                       float2 *__restrict__ rowstat, int S, int S_pad, int D, long long n_rows) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+    for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows;
+         r += warps) {
+        const long long bh = r / S_pad;
+        const int n = static_cast<int>(r - bh * S_pad);
+        if (n >= S) {
+            if (lane == 0) rowstat[r] = make_float2(0.f, 0.f);
+            continue;
+        }
+        const size_t row = static_cast<size_t>(bh) * S + n;
+        const T *dr = dout + row * D;
+        const float *orow = o32 + row * D;
+        float acc = 0.f;
+        for (int d = lane; d < D; d += 32) acc = fmaf(Elem<T>::to_float(dr[d]), orow[d], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            const float mt = load_f<T>(m_in, row);
+            const float lt = load_f<T>(l_in, row);
+            const float f = expf(m32[row] - mt) * (l32[row] / lt);
+            rowstat[r] = make_float2(mt * kLog2e + log2f(lt), f * acc);
+        }
+    }
+}
+
+// Writes 32 fp32 columns (times `mul`) of one tile row as 16-bit values into a
+// [128 rows][D] tile laid out as the TMA tensor map's 128-byte-swizzled boxes.
+template <bool BF16>
+__device__ __forceinline__ void stage_row32(uint8_t *tile, int row, int cc, const uint32_t (&o)[32], float mul) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+        pk[t] = ptx::pack2<BF16>(__uint_as_float(o[2 * t]) * mul, __uint_as_float(o[2 * t + 1]) * mul);
+    uint8_t *box = tile + (cc >> 1) * kBoxBytes + row * 128;
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+        const int chunk = (cc & 1) * 4 + q4;
+        *reinterpret_cast<uint4 *>(box + ((chunk ^ (row & 7)) * 16)) =
+            make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+    }
+}
+
+// ============================================================== dQ kernel
+template <int D>
+struct CfgQ {
+    static_assert(D == 64 || D == 128, "head size 64 or 128");
+    static constexpr int kBoxes = D / kBoxCols;
+    static constexpr int kTile = kBoxes * kBoxBytes;
+    static constexpr int kStages = (D == 64) ? 4 : 2;  // (K, V) tile pairs in flight
+    static constexpr int kOffQ = 0;
+    static constexpr int kOffDO = kTile;
+    static constexpr int kOffRing = 2 * kTile;  // stage s: K at +2 s kTile, V at +(2 s + 1) kTile
+    static constexpr int kOffBars = kOffRing + 2 * kStages * kTile;
+    static constexpr int kNumBars = 1 + 2 * kStages + 5;
+    static constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_dq, const Params p) {
+    using namespace ptx;
+    using C = CfgQ<D>;
+    constexpr int NS = C::kStages;
+    constexpr int TILE = C::kTile;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t *sQ = smem + C::kOffQ;
+    uint8_t *sDO = smem + C::kOffDO;
+    uint8_t *sRing = smem + C::kOffRing;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kOffBars);
+    uint64_t *qd_full = bars;
+    uint64_t *kv_full = bars + 1;      // [NS]
+    uint64_t *kv_empty = kv_full + NS;  // [NS]
+    uint64_t *sd_full = kv_empty + NS;
+    uint64_t *p_full = sd_full + 1;
+    uint64_t *acc_full = p_full + 1;
+    uint64_t *mma_done = acc_full + 1;
+    uint64_t *staged = mma_done + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(staged + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int bid = blockIdx.x;
+    const int qt = p.causal ? (p.n_qt - 1 - bid / p.BH) : (bid / p.BH);  // heaviest tiles first
+    const int bh = bid % p.BH;
+    const int n_kv = p.causal ? qt + 1 : p.n_qt;
+
+    if (threadIdx.x == 0) {
+        mbar_init(qd_full, 1);
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(sd_full, 1);
+        mbar_init(p_full, 4);
+        mbar_init(acc_full, 1);
+        mbar_init(mma_done, 1);
+        mbar_init(staged, 4);
+        *abort_flag = (*reinterpret_cast<volatile unsigned int *>(&g_device_error) != 0u) ? 1 : 0;
+        fence_mbarrier_init();
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const bool skip = *abort_flag != 0;
+
+    if (skip) {
+        // fall through to the teardown
+    } else if (warp == kWarpTma) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_q);
+            tma_prefetch_desc(&tm_k);
+            tma_prefetch_desc(&tm_v);
+            tma_prefetch_desc(&tm_do);
+            mbar_arrive_expect_tx(qd_full, 2 * TILE);
+            for (int b = 0; b < C::kBoxes; ++b) {
+                tma_load_3d(sQ + b * kBoxBytes, &tm_q, qd_full, b * kBoxCols, qt * 128, bh);
+                tma_load_3d(sDO + b * kBoxBytes, &tm_do, qd_full, b * kBoxCols, qt * 128, bh);
+            }
+            int issued = 0;
+            for (int t = 0; t < n_kv; ++t) {
+                const int s = t % NS;
+                if (t >= NS && !mbar_wait(&kv_empty[s], ((t / NS) - 1) & 1, abort_flag)) break;
+                uint8_t *sk = sRing + 2 * s * TILE;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * TILE);
+                for (int b = 0; b < C::kBoxes; ++b) {
+                    tma_load_3d(sk + b * kBoxBytes, &tm_k, &kv_full[s], b * kBoxCols, t * 128, bh);
+                    tma_load_3d(sk + TILE + b * kBoxBytes, &tm_v, &kv_full[s], b * kBoxCols, t * 128, bh);
+                }
+                issued = t + 1;
+            }
+            if (*abort_flag) {
+                volatile int never = 0;
+                mbar_wait(qd_full, 0, &never);
+                for (int t = max(0, issued - NS); t < issued; ++t) mbar_wait(&kv_full[t % NS], (t / NS) & 1, &never);
+            }
+        }
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            constexpr uint32_t kIdS = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+            constexpr uint32_t kIdAcc = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
+            const uint32_t q_addr = smem_u32(sQ);
+            const uint32_t do_addr = smem_u32(sDO);
+            // dQ += dS(t) K_t: dS from tensor memory, K_t (keys x D, D contiguous) as an MN-major B.
+            auto issue_dq = [&](int t) {
+                const int s = t % NS;
+                const uint32_t k_addr = smem_u32(sRing + 2 * s * TILE);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(tmem + kColAcc, tmem + kColS + kk * 8, smem_desc_sw128(k_addr + kk * 2048, kBoxBytes, 1024),
+                           kIdAcc, (t > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&kv_empty[s]);
+            };
+            bool ok = mbar_wait(qd_full, 0, abort_flag);
+            for (int t = 0; ok && t < n_kv; ++t) {
+                const int s = t % NS;
+                if (!(ok = mbar_wait(&kv_full[s], (t / NS) & 1, abort_flag))) break;
+                if (t > 0) {
+                    // dS(t-1) is in tensor memory and S, dP have been read.
+                    if (!(ok = mbar_wait(p_full, (t - 1) & 1, abort_flag))) break;
+                    tc_fence_after();
+                    issue_dq(t - 1);
+                }
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(sRing + 2 * s * TILE);
+                const uint32_t v_addr = k_addr + TILE;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tmem + kColS, smem_desc_sw128(q_addr + off, 16, 1024),
+                           smem_desc_sw128(k_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+                }
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tmem + kColDP, smem_desc_sw128(do_addr + off, 16, 1024),
+                           smem_desc_sw128(v_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(sd_full);
+            }
+            if (ok && n_kv > 0 && (ok = mbar_wait(p_full, (n_kv - 1) & 1, abort_flag))) {
+                tc_fence_after();
+                issue_dq(n_kv - 1);
+                mma_commit(acc_full);
+            }
+            mma_commit(mma_done);
+            volatile int never = 0;
+            mbar_wait(mma_done, 0, &never);
+        }
+    } else {
+        // ------------------------------------------------------------ elementwise warps 0-3
+        const int r = warp * 32 + lane;  // tile row == tensor-memory lane
+        const int row = qt * 128 + r;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        float b = 0.f, delta = 0.f;
+        if (row < p.S) {
+            const float2 st = p.rowstat[static_cast<size_t>(bh) * p.S_pad + row];
+            b = st.x;
+            delta = st.y;
+        }
+        const float c2 = p.scale_log2;
+        const float2 nd2 = make_float2(-delta, -delta);
+        bool ok = true;
+        for (int t = 0; t < n_kv; ++t) {
+            if (!(ok = mbar_wait_warp(sd_full, t & 1, abort_flag))) break;
+            tc_fence_after();
+            int lim = p.S - t * 128;  // keys [lim, 128) of this tile are masked for this row
+            if (p.causal) lim = min(lim, row - t * 128 + 1);
+            const bool masked = __any_sync(0xffffffffu, lim < 128);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t sv[32], dv[32];
+                tmem_ld32(lane_base + kColS + c * 32, sv);
+                tmem_ld32(lane_base + kColDP + c * 32, dv);
+                tmem_wait_ld();
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float s0 = __uint_as_float(sv[2 * i]), s1 = __uint_as_float(sv[2 * i + 1]);
+                    if (masked) {
+                        if (c * 32 + 2 * i >= lim) s0 = -INFINITY;
+                        if (c * 32 + 2 * i + 1 >= lim) s1 = -INFINITY;
+                    }
+                    const float2 e = make_float2(ex2_approx(fmaf(s0, c2, -b)), ex2_approx(fmaf(s1, c2, -b)));
+                    const float2 g =
+                        mul2(e, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), nd2));
+                    w[i] = pack2<BF16>(g.x, g.y);
+                }
+                // Columns [16c, 16c + 16) of S were read in this or an earlier chunk.
+                tmem_st16(lane_base + kColS + c * 16, w);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        if (ok) ok = mbar_wait_warp(acc_full, 0, abort_flag);
+        if (ok) {
+            tc_fence_after();
+            // Every MMA has completed: Q's shared memory stages the dQ tile.
+#pragma unroll
+            for (int cc = 0; cc < D / 32; ++cc) {
+                uint32_t o[32];
+                tmem_ld32(lane_base + kColAcc + cc * 32, o);
+                tmem_wait_ld();
+                stage_row32<BF16>(sQ, r, cc, o, p.scale);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(staged);
+            if (threadIdx.x == 0 && mbar_wait(staged, 0, abort_flag)) {
+                for (int bx = 0; bx < C::kBoxes; ++bx)
+                    tma_store_3d(&tm_dq, sQ + bx * kBoxBytes, bx * kBoxCols, qt * 128, bh);
+                tma_store_commit();
+                tma_store_wait_read0();
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort_flag && !skip) report_device_error(PMKL_DEVERR_TIMEOUT);
+}
+
+// ============================================================== dK, dV kernel
+template <int D>
+struct CfgKV {
+    static_assert(D == 64 || D == 128, "head size 64 or 128");
+    static constexpr int kBoxes = D / kBoxCols;
+    static constexpr int kTile = kBoxes * kBoxBytes;
+    static constexpr int kStages = (D == 64) ? 4 : 2;    // (Q, dO, row stats) in flight
+    static constexpr int kStage = 2 * kTile + kStatBytes;  // a multiple of 1024
+    static constexpr int kOffK = 0;
+    static constexpr int kOffV = kTile;
+    static constexpr int kOffRing = 2 * kTile;
+    static constexpr int kOffBars = kOffRing + kStages * kStage;
+    static constexpr int kNumBars = 1 + 2 * kStages + 5;
+    static constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
+    static_assert(kStage % 1024 == 0, "stage alignment");
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                        const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
+                        const Params p) {
+    using namespace ptx;
+    using C = CfgKV<D>;
+    constexpr int NS = C::kStages;
+    constexpr int TILE = C::kTile;
+    constexpr int STAGE = C::kStage;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t *sK = smem + C::kOffK;
+    uint8_t *sV = smem + C::kOffV;
+    uint8_t *sRing = smem + C::kOffRing;  // stage s: Q, dO, (b, delta)[128]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kOffBars);
+    uint64_t *kv_full = bars;
+    uint64_t *qd_full = bars + 1;       // [NS]
+    uint64_t *qd_empty = qd_full + NS;  // [NS]
+    uint64_t *sd_full = qd_empty + NS;
+    uint64_t *p_full = sd_full + 1;
+    uint64_t *acc_full = p_full + 1;
+    uint64_t *mma_done = acc_full + 1;
+    uint64_t *staged = mma_done + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(staged + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int bid = blockIdx.x;
+    const int kt = bid / p.BH;  // causal: key tile 0 meets every query tile, so ascending = heaviest first
+    const int bh = bid % p.BH;
+    const int i0 = p.causal ? kt : 0;
+    const int n_q = p.n_qt - i0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(kv_full, 1);
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&qd_full[s], 1);
+            mbar_init(&qd_empty[s], 1);
+        }
+        mbar_init(sd_full, 1);
+        mbar_init(p_full, 4);
+        mbar_init(acc_full, 1);
+        mbar_init(mma_done, 1);
+        mbar_init(staged, 4);
+        *abort_flag = (*reinterpret_cast<volatile unsigned int *>(&g_device_error) != 0u) ? 1 : 0;
+        fence_mbarrier_init();
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const bool skip = *abort_flag != 0;
+
+    if (skip) {
+        // fall through to the teardown
+    } else if (warp == kWarpTma) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_q);
+            tma_prefetch_desc(&tm_k);
+            tma_prefetch_desc(&tm_v);
+            tma_prefetch_desc(&tm_do);
+            mbar_arrive_expect_tx(kv_full, 2 * TILE);
+            for (int b = 0; b < C::kBoxes; ++b) {
+                tma_load_3d(sK + b * kBoxBytes, &tm_k, kv_full, b * kBoxCols, kt * 128, bh);
+                tma_load_3d(sV + b * kBoxBytes, &tm_v, kv_full, b * kBoxCols, kt * 128, bh);
+            }
+            int issued = 0;
+            for (int x = 0; x < n_q; ++x) {
+                const int s = x % NS;
+                const int i = i0 + x;
+                if (x >= NS && !mbar_wait(&qd_empty[s], ((x / NS) - 1) & 1, abort_flag)) break;
+                uint8_t *st = sRing + s * STAGE;
+                mbar_arrive_expect_tx(&qd_full[s], 2 * TILE + kStatBytes);
+                for (int b = 0; b < C::kBoxes; ++b) {
+                    tma_load_3d(st + b * kBoxBytes, &tm_q, &qd_full[s], b * kBoxCols, i * 128, bh);
+                    tma_load_3d(st + TILE + b * kBoxBytes, &tm_do, &qd_full[s], b * kBoxCols, i * 128, bh);
+                }
+                bulk_load(st + 2 * TILE, p.rowstat + static_cast<size_t>(bh) * p.S_pad + i * 128, kStatBytes,
+                          &qd_full[s]);
+                issued = x + 1;
+            }
+            if (*abort_flag) {
+                volatile int never = 0;
+                mbar_wait(kv_full, 0, &never);
+                for (int x = max(0, issued - NS); x < issued; ++x) mbar_wait(&qd_full[x % NS], (x / NS) & 1, &never);
+            }
+        }
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            constexpr uint32_t kIdS = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+            constexpr uint32_t kIdAcc = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
+            const uint32_t k_addr = smem_u32(sK);
+            const uint32_t v_addr = smem_u32(sV);
+            // dV += P^T(x) dO_x and dK += dS^T(x) Q_x: A from tensor memory, the
+            // query-tile operands (queries x D, D contiguous) as MN-major B.
+            auto issue_grads = [&](int x) {
+                const int s = x % NS;
+                const uint32_t q_addr = smem_u32(sRing + s * STAGE);
+                const uint32_t do_addr = q_addr + TILE;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(tmem + kColAcc, tmem + kColS + kk * 8, smem_desc_sw128(do_addr + kk * 2048, kBoxBytes, 1024),
+                           kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(tmem + kColAcc + D, tmem + kColDP + kk * 8,
+                           smem_desc_sw128(q_addr + kk * 2048, kBoxBytes, 1024), kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&qd_empty[s]);
+            };
+            bool ok = mbar_wait(kv_full, 0, abort_flag);
+            for (int x = 0; ok && x < n_q; ++x) {
+                const int s = x % NS;
+                if (!(ok = mbar_wait(&qd_full[s], (x / NS) & 1, abort_flag))) break;
+                if (x > 0) {
+                    if (!(ok = mbar_wait(p_full, (x - 1) & 1, abort_flag))) break;
+                    tc_fence_after();
+                    issue_grads(x - 1);
+                }
+                tc_fence_after();
+                const uint32_t q_addr = smem_u32(sRing + s * STAGE);
+                const uint32_t do_addr = q_addr + TILE;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tmem + kColS, smem_desc_sw128(k_addr + off, 16, 1024),
+                           smem_desc_sw128(q_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+                }
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tmem + kColDP, smem_desc_sw128(v_addr + off, 16, 1024),
+                           smem_desc_sw128(do_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(sd_full);
+            }
+            if (ok && n_q > 0 && (ok = mbar_wait(p_full, (n_q - 1) & 1, abort_flag))) {
+                tc_fence_after();
+                issue_grads(n_q - 1);
+                mma_commit(acc_full);
+            }
+            mma_commit(mma_done);
+            volatile int never = 0;
+            mbar_wait(mma_done, 0, &never);
+        }
+    } else {
+        // ------------------------------------------------------------ elementwise warps 0-3
+        const int r = warp * 32 + lane;  // key row of the tile == tensor-memory lane
+        const int key = kt * 128 + r;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        const float c2 = p.scale_log2;
+        bool ok = true;
+        for (int x = 0; x < n_q; ++x) {
+            if (!(ok = mbar_wait_warp(sd_full, x & 1, abort_flag))) break;
+            tc_fence_after();
+            const float4 *st = reinterpret_cast<const float4 *>(sRing + (x % NS) * STAGE + 2 * TILE);
+            const int qbase = (i0 + x) * 128;
+            const int lo = p.causal ? key - qbase : 0;  // queries [0, lo) precede this key
+            const int hi = p.S - qbase;                  // queries [hi, 128) are past the end
+            const bool masked = __any_sync(0xffffffffu, lo > 0 || hi < 128);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t sv[32], dv[32];
+                tmem_ld32(lane_base + kColS + c * 32, sv);
+                tmem_ld32(lane_base + kColDP + c * 32, dv);
+                tmem_wait_ld();
+                uint32_t wp[16], wd[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int n0 = c * 32 + 2 * i;
+                    const float4 bd = st[n0 >> 1];  // (b, delta) of queries n0, n0 + 1
+                    float s0 = __uint_as_float(sv[2 * i]), s1 = __uint_as_float(sv[2 * i + 1]);
+                    if (masked) {
+                        if (n0 < lo || n0 >= hi) s0 = -INFINITY;
+                        if (n0 + 1 < lo || n0 + 1 >= hi) s1 = -INFINITY;
+                    }
+                    const float2 pp = make_float2(ex2_approx(fmaf(s0, c2, -bd.x)), ex2_approx(fmaf(s1, c2, -bd.z)));
+                    const float2 g = mul2(pp, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])),
+                                                   make_float2(-bd.y, -bd.w)));
+                    wp[i] = pack2<BF16>(pp.x, pp.y);
+                    wd[i] = pack2<BF16>(g.x, g.y);
+                }
+                tmem_st16(lane_base + kColS + c * 16, wp);
+                tmem_st16(lane_base + kColDP + c * 16, wd);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        if (ok) ok = mbar_wait_warp(acc_full, 0, abort_flag);
+        if (ok) {
+            tc_fence_after();
+            // Every MMA has completed: K's and V's shared memory stage dV and dK.
+#pragma unroll
+            for (int cc = 0; cc < D / 32; ++cc) {
+                uint32_t o[32];
+                tmem_ld32(lane_base + kColAcc + cc * 32, o);
+                tmem_wait_ld();
+                stage_row32<BF16>(sK, r, cc, o, 1.f);
+                tmem_ld32(lane_base + kColAcc + D + cc * 32, o);
+                tmem_wait_ld();
+                stage_row32<BF16>(sV, r, cc, o, p.scale);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(staged);
+            if (threadIdx.x == 0 && mbar_wait(staged, 0, abort_flag)) {
+                for (int bx = 0; bx < C::kBoxes; ++bx) {
+                    tma_store_3d(&tm_dv, sK + bx * kBoxBytes, bx * kBoxCols, kt * 128, bh);
+                    tma_store_3d(&tm_dk, sV + bx * kBoxBytes, bx * kBoxCols, kt * 128, bh);
+                }
+                tma_store_commit();
+                tma_store_wait_read0();
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort_flag && !skip) report_device_error(PMKL_DEVERR_TIMEOUT);
+}
+
+}  // namespace bwd
+}  // namespace pmkl_b200

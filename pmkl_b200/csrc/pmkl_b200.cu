@@ -15,6 +15,8 @@
 #include <cstdint>
 #include <mutex>
 
+#include "attention_bwd.cuh"
+#include "attention_bwd_simt.cuh"
 #include "attention_simt.cuh"
 #include "attention_pp.cuh"
 #include "attention_tc.cuh"
@@ -304,6 +306,189 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     return launch_simt<__nv_bfloat16>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, stream);
 }
 
+// ------------------------------------------------------------------ backward
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Workspace of the tensor-core backward: the forward's fp32 O, m, l, then the
+// per-row (b, delta) pairs at a row pitch of S rounded up to 128.
+struct BwdLayout {
+    size_t o, m, l, rowstat, total;
+    int S_pad;
+};
+
+BwdLayout bwd_layout_tc(long long BH, int S, int D) {
+    BwdLayout L;
+    L.S_pad = ((S + 127) / 128) * 128;
+    size_t off = 0;
+    L.o = off;
+    off = align256(off + static_cast<size_t>(BH) * S * D * 4);
+    L.m = off;
+    off = align256(off + static_cast<size_t>(BH) * S * 4);
+    L.l = off;
+    off = align256(off + static_cast<size_t>(BH) * S * 4);
+    L.rowstat = off;
+    off = align256(off + static_cast<size_t>(BH) * L.S_pad * 8);
+    L.total = off;
+    return L;
+}
+
+// Workspace of the CUDA-core backward: delta per row.
+size_t bwd_ws_simt(long long BH, int S) { return align256(static_cast<size_t>(BH) * S * 4); }
+
+bool bwd_tc_applies(const void *const (&ptrs)[9], int D, int dtype) {
+    if (dtype != PMKL_DTYPE_F16 && dtype != PMKL_DTYPE_BF16) return false;
+    if (D != 64 && D != 128) return false;
+    for (const void *p : ptrs)
+        if (!aligned16(p)) return false;
+    return true;
+}
+
+template <typename T>
+int launch_bwd_rowstat(const void *dout, const float *o32, const float *m32, const float *l32, const void *m_in,
+                       const void *l_in, float2 *rowstat, int S, int S_pad, int D, long long BH,
+                       cudaStream_t stream) {
+    const long long n_rows = BH * S_pad;
+    long long blocks = (n_rows + 7) / 8;
+    const long long cap = static_cast<long long>(sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    bwd::bwd_rowstat_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const T *>(dout), o32, m32, l32, m_in, l_in, rowstat, S, S_pad, D, n_rows);
+    return launch_status();
+}
+
+template <int D, bool BF16>
+int launch_bwd_tc(const void *dout, const void *q, const void *k, const void *v, void *dq, void *dk, void *dv, int S,
+                  int BH, int causal, float scale, int dtype, const float2 *rowstat, int S_pad, cudaStream_t stream) {
+    static std::once_flag once_q[kMaxDevices], once_kv[kMaxDevices];
+    auto kq = bwd::attn_bwd_dq_kernel<D, BF16>;
+    auto kkv = bwd::attn_bwd_dkv_kernel<D, BF16>;
+    constexpr int smem_q = bwd::CfgQ<D>::kSmemBytes;
+    constexpr int smem_kv = bwd::CfgKV<D>::kSmemBytes;
+    if (!ensure_smem(kq, smem_q, once_q) || !ensure_smem(kkv, smem_kv, once_kv)) return PMKL_ERR_LAUNCH;
+    CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
+    if (!make_tile_map(&tq, q, dtype, D, S, BH) || !make_tile_map(&tk, k, dtype, D, S, BH) ||
+        !make_tile_map(&tv, v, dtype, D, S, BH) || !make_tile_map(&tdo, dout, dtype, D, S, BH) ||
+        !make_tile_map(&tdq, dq, dtype, D, S, BH) || !make_tile_map(&tdk, dk, dtype, D, S, BH) ||
+        !make_tile_map(&tdv, dv, dtype, D, S, BH))
+        return PMKL_ERR_LAUNCH;
+    bwd::Params p;
+    p.S = S;
+    p.S_pad = S_pad;
+    p.BH = BH;
+    p.n_qt = (S + 127) / 128;
+    p.causal = causal;
+    p.scale = scale;
+    p.scale_log2 = scale * bwd::kLog2e;
+    p.rowstat = rowstat;
+    const long long blocks = static_cast<long long>(p.n_qt) * BH;
+    if (blocks > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    kq<<<static_cast<unsigned>(blocks), bwd::kThreads, smem_q, stream>>>(tq, tk, tv, tdo, tdq, p);
+    const int rc = launch_status();
+    if (rc != PMKL_OK) return rc;
+    kkv<<<static_cast<unsigned>(blocks), bwd::kThreads, smem_kv, stream>>>(tq, tk, tv, tdo, tdk, tdv, p);
+    return launch_status();
+}
+
+template <typename T, int DMAX>
+int launch_bwd_simt_t(const void *dout, const void *q, const void *k, const void *v, const void *m, const void *l,
+                      void *dq, void *dk, void *dv, float *delta, int S, int D, int BH, int causal, float scale,
+                      cudaStream_t stream) {
+    static std::once_flag once_q[kMaxDevices], once_kv[kMaxDevices];
+    auto kq = simt::attn_bwd_simt_q_kernel<T, DMAX>;
+    auto kkv = simt::attn_bwd_simt_kv_kernel<T, DMAX>;
+    constexpr int smem = simt::bwd_smem_bytes<DMAX>();
+    if (!ensure_smem(kq, smem, once_q) || !ensure_smem(kkv, smem, once_kv)) return PMKL_ERR_LAUNCH;
+    const int n_t = (S + 31) / 32;
+    const long long blocks = static_cast<long long>(n_t) * BH;
+    if (blocks > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    const T *tdo = static_cast<const T *>(dout), *tq = static_cast<const T *>(q), *tk = static_cast<const T *>(k),
+            *tv = static_cast<const T *>(v), *tm = static_cast<const T *>(m), *tl = static_cast<const T *>(l);
+    kq<<<static_cast<unsigned>(blocks), simt::kThreads, smem, stream>>>(tdo, tq, tk, tv, tm, tl, static_cast<T *>(dq),
+                                                                        delta, S, D, BH, n_t, causal, scale);
+    const int rc = launch_status();
+    if (rc != PMKL_OK) return rc;
+    kkv<<<static_cast<unsigned>(blocks), simt::kThreads, smem, stream>>>(
+        tdo, tq, tk, tv, tm, tl, delta, static_cast<T *>(dk), static_cast<T *>(dv), S, D, BH, causal, scale);
+    return launch_status();
+}
+
+template <typename T>
+int launch_bwd_simt(const void *dout, const void *q, const void *k, const void *v, const void *m, const void *l,
+                    void *dq, void *dk, void *dv, float *delta, int S, int D, int BH, int causal, float scale,
+                    cudaStream_t stream) {
+    if (D <= 32) return launch_bwd_simt_t<T, 32>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
+    if (D <= 64) return launch_bwd_simt_t<T, 64>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
+    if (D <= 128)
+        return launch_bwd_simt_t<T, 128>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
+    return launch_bwd_simt_t<T, 256>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
+}
+
+size_t bwd_workspace_size(long long BH, int S, int D, int dtype) {
+    const bool tc_shape = (dtype == PMKL_DTYPE_F16 || dtype == PMKL_DTYPE_BF16) && (D == 64 || D == 128);
+    const size_t simt_bytes = bwd_ws_simt(BH, S);
+    if (!tc_shape) return simt_bytes;
+    const size_t tc_bytes = bwd_layout_tc(BH, S, D).total;
+    return tc_bytes > simt_bytes ? tc_bytes : simt_bytes;
+}
+
+int attention_bwd_impl(const void *dout, const void *q, const void *k, const void *v, const void *m, const void *l,
+                       void *dq, void *dk, void *dv, int batch, int heads, int seq, int hidden, int dtype,
+                       int is_causal, float scale, void *workspace, size_t workspace_bytes, int kernel,
+                       void *stream_) {
+    if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
+    if (!dtype_valid(dtype)) return PMKL_ERR_INVALID_DTYPE;
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05)
+        return PMKL_ERR_UNSUPPORTED;
+    const long long BH = static_cast<long long>(batch) * heads;
+    if (BH == 0 || seq == 0 || hidden == 0) return PMKL_OK;
+    if (hidden > 256) return PMKL_ERR_UNSUPPORTED;
+    if (BH > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    if (!dout || !q || !k || !v || !m || !l || !dq || !dk || !dv || !workspace) return PMKL_ERR_NULL_POINTER;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PMKL_ERR_MISALIGNED;
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    const float sc = (scale > 0.f) ? scale : 1.0f / sqrtf(static_cast<float>(hidden));
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const int causal = is_causal ? 1 : 0;
+    const int bh = static_cast<int>(BH);
+    const void *const ptrs[9] = {dout, q, k, v, m, l, dq, dk, dv};
+    const bool tc_ok = bwd_tc_applies(ptrs, hidden, dtype);
+    if (kernel == PMKL_ATTN_TCGEN05 && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if (tc_ok && kernel != PMKL_ATTN_SIMT) {
+        const BwdLayout L = bwd_layout_tc(BH, seq, hidden);
+        if (workspace_bytes < L.total) return PMKL_ERR_WORKSPACE;
+        uint8_t *ws = static_cast<uint8_t *>(workspace);
+        float *o32 = reinterpret_cast<float *>(ws + L.o);
+        float *m32 = reinterpret_cast<float *>(ws + L.m);
+        float *l32 = reinterpret_cast<float *>(ws + L.l);
+        float2 *rowstat = reinterpret_cast<float2 *>(ws + L.rowstat);
+        // The forward, with fp32 outputs, gives delta = sum_j p dP through dO . O.
+        int rc = attention_impl(q, k, v, o32, m32, l32, batch, heads, seq, hidden, dtype, PMKL_DTYPE_F32, causal, sc,
+                                PMKL_ATTN_AUTO, stream_);
+        if (rc != PMKL_OK) return rc;
+        rc = dtype == PMKL_DTYPE_BF16
+                 ? launch_bwd_rowstat<__nv_bfloat16>(dout, o32, m32, l32, m, l, rowstat, seq, L.S_pad, hidden, BH, stream)
+                 : launch_bwd_rowstat<__half>(dout, o32, m32, l32, m, l, rowstat, seq, L.S_pad, hidden, BH, stream);
+        if (rc != PMKL_OK) return rc;
+        if (dtype == PMKL_DTYPE_BF16)
+            return hidden == 64 ? launch_bwd_tc<64, true>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype,
+                                                          rowstat, L.S_pad, stream)
+                                : launch_bwd_tc<128, true>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype,
+                                                           rowstat, L.S_pad, stream);
+        return hidden == 64 ? launch_bwd_tc<64, false>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype, rowstat,
+                                                       L.S_pad, stream)
+                            : launch_bwd_tc<128, false>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype, rowstat,
+                                                        L.S_pad, stream);
+    }
+    if (workspace_bytes < bwd_ws_simt(BH, seq)) return PMKL_ERR_WORKSPACE;
+    float *delta = static_cast<float *>(workspace);
+    if (dtype == PMKL_DTYPE_F32)
+        return launch_bwd_simt<float>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, stream);
+    if (dtype == PMKL_DTYPE_F16)
+        return launch_bwd_simt<__half>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, stream);
+    return launch_bwd_simt<__nv_bfloat16>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, stream);
+}
+
 // ------------------------------------------------------------------ softmax launchers
 template <bool LOG>
 int launch_softmax_vec(float *dst, const float *src, int elements, int stride, int rows, cudaStream_t stream) {
@@ -384,6 +569,27 @@ int pmkl_causal_attention_fwd_ex(const void *q, const void *k, const void *v, vo
                           stream);
 }
 
+int pmkl_causal_attention_bwd(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                              const void *l, void *dq, void *dk, void *dv, int batch, int heads, int seq,
+                              int hidden, int dtype, int is_causal, float scale, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+    return attention_bwd_impl(dout, q, k, v, m, l, dq, dk, dv, batch, heads, seq, hidden, dtype, is_causal, scale,
+                              workspace, workspace_bytes, PMKL_ATTN_AUTO, stream);
+}
+
+int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                                 const void *l, void *dq, void *dk, void *dv, int batch, int heads, int seq,
+                                 int hidden, int dtype, int is_causal, float scale, void *workspace,
+                                 size_t workspace_bytes, int kernel, void *stream) {
+    return attention_bwd_impl(dout, q, k, v, m, l, dq, dk, dv, batch, heads, seq, hidden, dtype, is_causal, scale,
+                              workspace, workspace_bytes, kernel, stream);
+}
+
+size_t pmkl_causal_attention_bwd_workspace_size(int batch, int heads, int seq, int hidden, int dtype) {
+    if (batch <= 0 || heads <= 0 || seq <= 0 || hidden <= 0 || !dtype_valid(dtype)) return 0;
+    return bwd_workspace_size(static_cast<long long>(batch) * heads, seq, hidden, dtype);
+}
+
 int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
                                    int out_dtype, int kernel) {
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
@@ -437,6 +643,8 @@ const char *pmkl_status_string(int status) {
             return "PMKL_ERR_LAUNCH: CUDA launch failed";
         case PMKL_ERR_DEVICE_TIMEOUT:
             return "PMKL_ERR_DEVICE_TIMEOUT: a kernel abandoned a bounded wait";
+        case PMKL_ERR_WORKSPACE:
+            return "PMKL_ERR_WORKSPACE: workspace too small";
         default:
             return "PMKL_ERR_UNKNOWN";
     }

@@ -84,21 +84,70 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> fused_self_attention_fw_ex(const 
     return forward_impl(q, k, v, is_causal, out_fp32, kernel, scale);
 }
 
-// fused_self_attention.cpp:175 -- same name and arguments.  The B200 build
-// has no backward kernel yet.
+namespace {
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> backward_impl(const at::Tensor &dout, const at::Tensor &q,
+                                                             const at::Tensor &k, const at::Tensor &v,
+                                                             const at::Tensor &out_m, const at::Tensor &out_l,
+                                                             bool is_causal, int64_t kernel, double scale) {
+    // fused_self_attention.cpp:178-180
+    TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "Input tensor shapes must match");
+    TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "Input tensor must be contiguous");
+    TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(), "Input tensor shapes must match");
+    check_inputs(q, k, v);
+    TORCH_CHECK(dout.sizes() == q.sizes(), "fused_self_attention_bw: grad_output must have q's shape");
+    const std::vector<int64_t> stat_shape = {q.size(0), q.size(1), q.size(2)};
+    TORCH_CHECK(out_m.sizes() == stat_shape && out_l.sizes() == stat_shape,
+                "fused_self_attention_bw: out_m and out_l must be [batch, heads, seq]");
+    for (const at::Tensor *t : {&dout, &out_m, &out_l}) {
+        TORCH_CHECK(t->device() == q.device(), "fused_self_attention_bw: all tensors must be on q's device");
+        // The reference reads them as v's scalar type (fused_self_attention.cpp:205-209).
+        TORCH_CHECK(t->scalar_type() == v.scalar_type(), "fused_self_attention_bw: grad_output, out_m and out_l "
+                    "must have v's dtype");
+    }
+    const c10::cuda::CUDAGuard guard(q.device());
+    const int B = static_cast<int>(q.size(0)), H = static_cast<int>(q.size(1));
+    const int S = static_cast<int>(q.size(2)), D = static_cast<int>(q.size(3));
+    const at::Tensor dc = dout.contiguous(), mc = out_m.contiguous(), lc = out_l.contiguous();
+    // Every element is written, so empty (not zeros, :186-188) gives the same result.
+    at::Tensor dq = at::empty_like(q), dk = at::empty_like(k), dv = at::empty_like(v);
+    const int dt = pmkl_dtype_of(v.scalar_type());
+    const size_t ws_bytes = pmkl_causal_attention_bwd_workspace_size(B, H, S, D, dt);
+    at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes > 0 ? ws_bytes : 1)}, q.options().dtype(at::kByte));
+    cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+    const int rc = pmkl_causal_attention_bwd_ex(dc.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                mc.data_ptr(), lc.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                                dv.data_ptr(), B, H, S, D, dt, is_causal ? 1 : 0,
+                                                static_cast<float>(scale), ws.data_ptr(), ws_bytes,
+                                                static_cast<int>(kernel), stream);
+    TORCH_CHECK(rc == PMKL_OK, "pmkl_causal_attention_bwd failed: ", pmkl_status_string(rc));
+    return std::make_tuple(dq, dk, dv);
+}
+
+}  // namespace
+
+// fused_self_attention.cpp:175 -- same name, arguments and return tuple.
 std::tuple<at::Tensor, at::Tensor, at::Tensor> fused_self_attention_bw(const at::Tensor &dout, const at::Tensor &q,
                                                                        const at::Tensor &k, const at::Tensor &v,
                                                                        const at::Tensor &out_m,
                                                                        const at::Tensor &out_l, bool is_causal) {
-    TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "Input tensor shapes must match");
-    TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(), "Input tensor shapes must match");
-    TORCH_CHECK_NOT_IMPLEMENTED(false, "fused_self_attention_bw: the B200 build has no backward kernel yet");
-    return std::make_tuple(at::Tensor(), at::Tensor(), at::Tensor());
+    return backward_impl(dout, q, k, v, out_m, out_l, is_causal, PMKL_ATTN_AUTO, 0.0);
+}
+
+// Extra entry (no reference counterpart): explicit kernel choice and scale.
+std::tuple<at::Tensor, at::Tensor, at::Tensor> fused_self_attention_bw_ex(
+    const at::Tensor &dout, const at::Tensor &q, const at::Tensor &k, const at::Tensor &v, const at::Tensor &out_m,
+    const at::Tensor &out_l, bool is_causal, int64_t kernel, double scale) {
+    return backward_impl(dout, q, k, v, out_m, out_l, is_causal, kernel, scale);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("fused_self_attention_fw", &fused_self_attention_fw, "fused_self_attention_fw");
     m.def("fused_self_attention_bw", &fused_self_attention_bw, "fused_self_attention_bw");
+    m.def("fused_self_attention_bw_ex", &fused_self_attention_bw_ex, "fused_self_attention_bw_ex",
+          pybind11::arg("dout"), pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("out_m"),
+          pybind11::arg("out_l"), pybind11::arg("is_causal"), pybind11::arg("kernel") = 0,
+          pybind11::arg("scale") = 0.0);
     m.def("fused_self_attention_fw_ex", &fused_self_attention_fw_ex, "fused_self_attention_fw_ex",
           pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("is_causal"),
           pybind11::arg("out_fp32") = false, pybind11::arg("kernel") = 0, pybind11::arg("scale") = 0.0);

@@ -10,9 +10,10 @@ Differences from the reference, all deliberate:
   raises ``NotImplementedError`` unless the tensors are on the CPU and
   ``debug`` is true, ``__init__.py:15-18``);
 * CPU tensors raise ``NotImplementedError``: this build has no CPU path;
-* the backward raises ``NotImplementedError`` on CUDA, as the reference's
-  does for any non-CPU tensor (``__init__.py:27-31``): there is no backward
-  kernel yet.
+* the backward runs the B200 backward kernels on CUDA tensors (the
+  reference's raises ``NotImplementedError`` for any non-CPU tensor,
+  ``__init__.py:27-31``).  Like the reference it ignores the gradients
+  arriving for ``out_m`` and ``out_l``.
 """
 import torch
 from torch.autograd import Function

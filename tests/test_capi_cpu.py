@@ -41,7 +41,7 @@ def test_version_and_status_strings():
     L = pmkl_b200.capi()
     assert L.pmkl_version() == 100
     assert L.pmkl_status_string(0) == b"PMKL_OK"
-    for code in range(-1, -9, -1):
+    for code in range(-1, -10, -1):
         assert L.pmkl_status_string(code).startswith(b"PMKL_ERR_")
     assert L.pmkl_status_string(-99) == b"PMKL_ERR_UNKNOWN"
 
@@ -72,6 +72,42 @@ def test_attention_empty_problem_is_ok_without_device():
     assert attn(L, B=0, ptrs=0) == 0
     assert attn(L, S=0, ptrs=0) == 0
     assert attn(L, H=0, ptrs=0) == 0
+
+
+def bwd(L, B=1, H=1, S=8, D=64, dtype=2, kernel=0, ptrs=FAKE, ws=0x100000, ws_bytes=1 << 30):
+    return L.pmkl_causal_attention_bwd_ex(*([ptrs] * 9), B, H, S, D, dtype, 1, 0.0, ws, ws_bytes, kernel, None)
+
+
+def test_backward_argument_errors():
+    L = pmkl_b200.capi()
+    assert bwd(L, B=-1) == -1
+    assert bwd(L, dtype=7) == -2
+    assert bwd(L, kernel=9) == -5
+    assert bwd(L, kernel=3) == -5  # no one-tile backward
+    assert bwd(L, D=300) == -5
+    assert bwd(L, ptrs=0) == -3
+    assert bwd(L, ws=0) == -3
+    assert bwd(L, ws=0x100010) == -4  # workspace must be 256-byte aligned
+    assert bwd(L, B=0, ptrs=0, ws=0) == 0  # empty: nothing to do
+    assert bwd(L, S=0, ptrs=0, ws=0) == 0
+
+
+def test_backward_workspace_size():
+    """Tensor-core layout: fp32 O, m, l of the forward plus (b, delta) pairs at a
+    row pitch of seq rounded up to 128, each region 256-byte aligned; the
+    CUDA-core path needs one fp32 delta per row."""
+    L = pmkl_b200.capi()
+    f = L.pmkl_causal_attention_bwd_workspace_size
+    a = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    B, H, S, D = 2, 3, 200, 128
+    BH = B * H
+    assert f(B, H, S, D, 2) == a(BH * S * D * 4) + 2 * a(BH * S * 4) + a(BH * 256 * 8)
+    assert f(B, H, S, 64, 1) == a(BH * S * 64 * 4) + 2 * a(BH * S * 4) + a(BH * 256 * 8)
+    assert f(B, H, S, 96, 2) == a(BH * S * 4)  # no tensor-core path for D = 96
+    assert f(B, H, S, D, 0) == a(BH * S * 4)  # fp32
+    assert f(0, H, S, D, 2) == 0 and f(B, H, 0, D, 2) == 0 and f(B, H, S, D, 9) == 0
+    # config 3 (bf16 B16 H32 S4096 D128): about 1.1 GB
+    assert 1.0e9 < f(16, 32, 4096, 128, 2) < 1.2e9
 
 
 def test_softmax_argument_errors():

@@ -89,11 +89,56 @@ def test_errors():
         pmkl_pytorch_ext.fused_self_attention_fw(*(torch.zeros(1, 1, 4, 300, device="cuda"),) * 3, True)
 
 
-def test_backward_not_implemented():
-    q, k, v = (t.cuda().requires_grad_() for t in seeded_qkv(1, 2, 16, 64, torch.bfloat16, seed=5))
-    out, _, _ = fused_self_attention(q, k, v, True)
-    with pytest.raises(NotImplementedError):
-        out.float().sum().backward()
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("is_causal", [False, True])
+@pytest.mark.parametrize("hidden_size", [64, 128])
+def test_backward_through_autograd_vs_sdpa(hidden_size, is_causal, dtype):
+    """The reference's test also backpropagates through both implementations
+    and compares q/k/v gradients (test_fused_self_attention.py:21-38); here the
+    reference side is float64 autograd through scaled_dot_product_attention,
+    with a bound per dtype."""
+    q, k, v = seeded_qkv(2, 16, 128, hidden_size, dtype, seed=hidden_size + 7 * is_causal)
+    g = torch.Generator().manual_seed(9)
+    dout = torch.randn(q.shape, generator=g).to(dtype)
+    qd, kd, vd = (t.cuda().requires_grad_() for t in (q, k, v))
+    out, _, _ = fused_self_attention(qd, kd, vd, is_causal)
+    out.backward(dout.cuda())
+    q64, k64, v64 = (t.double().requires_grad_() for t in (q, k, v))
+    F.scaled_dot_product_attention(q64, k64, v64, is_causal=is_causal).backward(dout.double())
+    # fp32: the reference's all_close scale.  16-bit: out_m and out_l come back
+    # in the 16-bit dtype (as the reference returns them) and the backward uses
+    # them as given, so each P entry is off exact math by up to (|m| + 1) 2^-8
+    # relative; P, dS and the gradients are also rounded to 16 bits.
+    tol = 2e-5 if dtype == torch.float32 else 3e-2
+    for got, ref in ((qd.grad, q64.grad), (kd.grad, k64.grad), (vd.grad, v64.grad)):
+        assert got.dtype == dtype
+        err = (got.double().cpu() - ref).abs().max().item()
+        assert err <= tol * ref.abs().max().item(), (err, ref.abs().max().item())
+
+
+def test_bw_matches_capi_bitwise():
+    q, k, v = (t.cuda() for t in seeded_qkv(1, 4, 300, 128, torch.bfloat16, seed=5))
+    out, m, l = pmkl_pytorch_ext.fused_self_attention_fw(q, k, v, True)
+    dout = torch.randn_like(out)
+    dq, dk, dv = pmkl_pytorch_ext.fused_self_attention_bw(dout, q, k, v, m, l, True)
+    ref = [torch.empty_like(q) for _ in range(3)]
+    pmkl_b200.attention_bwd(dout, q, k, v, m, l, *ref, True)
+    torch.cuda.synchronize()
+    for a, b in zip((dq, dk, dv), ref):
+        assert torch.equal(a, b)
+
+
+def test_bw_errors():
+    q = torch.randn(1, 2, 8, 64, device="cuda")
+    m = torch.zeros(1, 2, 8, device="cuda")
+    with pytest.raises(RuntimeError, match="contiguous"):
+        pmkl_pytorch_ext.fused_self_attention_bw(q, q.transpose(2, 3).contiguous().transpose(2, 3), q, q, m, m, True)
+    with pytest.raises(RuntimeError, match="v's dtype"):
+        pmkl_pytorch_ext.fused_self_attention_bw(q, q, q, q, m.half(), m, True)
+    with pytest.raises(RuntimeError, match="batch, heads, seq"):
+        pmkl_pytorch_ext.fused_self_attention_bw(q, q, q, q, m[:, :1], m, True)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pmkl_pytorch_ext.fused_self_attention_bw(q, q.cpu(), q.cpu(), q.cpu(), m, m, True)
 
 
 def test_empty_inputs():
