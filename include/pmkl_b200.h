@@ -144,6 +144,34 @@ int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k,
  * reference's CPU backward needs no scratch. */
 size_t pmkl_causal_attention_bwd_workspace_size(int batch, int heads, int seq, int hidden, int dtype);
 
+/* Size of the library's static device scratch used by
+ * pmkl_causal_attention_bwd_static (64 MiB per device). */
+#define PMKL_BWD_STATIC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/*
+ * pmkl_causal_attention_bwd without a caller workspace and without any device
+ * allocation: the scratch is a statically allocated __device__ array of
+ * PMKL_BWD_STATIC_SCRATCH_BYTES (256-byte aligned) inside libpmkl_b200, whose
+ * address is looked up once per device.  No cudaMalloc, cudaFree or allocator
+ * call happens on this path.  Same arguments (minus the workspace), results
+ * and status codes as pmkl_causal_attention_bwd; a problem whose
+ * pmkl_causal_attention_bwd_workspace_size() exceeds the scratch is rejected
+ * with PMKL_ERR_WORKSPACE before anything is launched.  Nothing in the scratch
+ * has to start at zero: every byte a kernel reads is written earlier in the
+ * same call.
+ *
+ * The scratch is shared by every call on a device: two calls whose work
+ * overlaps in time (different streams, or different host threads without
+ * ordering between their streams) race on it and give undefined results.
+ * Issue such calls on one stream, or order them.
+ *
+ * No reference counterpart: an addition of this library (the reference's
+ * backward is a host loop that needs no scratch).
+ */
+int pmkl_causal_attention_bwd_static(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                                     const void *l, void *dq, void *dk, void *dv, int batch, int heads, int seq,
+                                     int hidden, int dtype, int is_causal, float scale, void *stream);
+
 /*
  * Row-wise softmax / log-softmax.
  *

@@ -63,6 +63,8 @@ def capi() -> ctypes.CDLL:
         L.pmkl_causal_attention_bwd.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp, ctypes.c_size_t, vp]
         L.pmkl_causal_attention_bwd_ex.restype = i32
         L.pmkl_causal_attention_bwd_ex.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp, ctypes.c_size_t, i32, vp]
+        L.pmkl_causal_attention_bwd_static.restype = i32
+        L.pmkl_causal_attention_bwd_static.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp]
         L.pmkl_causal_attention_bwd_workspace_size.restype = ctypes.c_size_t
         L.pmkl_causal_attention_bwd_workspace_size.argtypes = [i32] * 5
         L.pmkl_warp_softmax_fwd.restype = i32

@@ -423,6 +423,34 @@ int launch_bwd_simt(const void *dout, const void *q, const void *k, const void *
     return launch_bwd_simt_t<T, 256>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
 }
 
+// Scratch of pmkl_causal_attention_bwd_static: static device memory of this
+// module, never allocated or freed by a call.  Its address is looked up once
+// per device.
+__device__ __align__(256) uint8_t g_bwd_static_scratch[PMKL_BWD_STATIC_SCRATCH_BYTES];
+
+struct StaticScratch {
+    std::once_flag once;
+    void *ptr = nullptr;
+};
+StaticScratch g_static_scratch[kMaxDevices];
+
+void *static_scratch() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    StaticScratch &s = g_static_scratch[dev];
+    std::call_once(s.once, [&]() {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_bwd_static_scratch) == cudaSuccess)
+            s.ptr = p;
+        else
+            cudaGetLastError();
+    });
+    return s.ptr;
+}
+
 size_t bwd_workspace_size(long long BH, int S, int D, int dtype) {
     const bool tc_shape = (dtype == PMKL_DTYPE_F16 || dtype == PMKL_DTYPE_BF16) && (D == 64 || D == 128);
     const size_t simt_bytes = bwd_ws_simt(BH, S);
@@ -583,6 +611,22 @@ int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k,
                                  size_t workspace_bytes, int kernel, void *stream) {
     return attention_bwd_impl(dout, q, k, v, m, l, dq, dk, dv, batch, heads, seq, hidden, dtype, is_causal, scale,
                               workspace, workspace_bytes, kernel, stream);
+}
+
+int pmkl_causal_attention_bwd_static(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                                     const void *l, void *dq, void *dk, void *dv, int batch, int heads, int seq,
+                                     int hidden, int dtype, int is_causal, float scale, void *stream) {
+    // Argument errors and empty problems first, as the workspace entry reports them.
+    if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
+    if (!dtype_valid(dtype)) return PMKL_ERR_INVALID_DTYPE;
+    if (static_cast<long long>(batch) * heads == 0 || seq == 0 || hidden == 0) return PMKL_OK;
+    if (hidden > 256) return PMKL_ERR_UNSUPPORTED;
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    void *ws = static_scratch();
+    if (!ws) return PMKL_ERR_LAUNCH;
+    return attention_bwd_impl(dout, q, k, v, m, l, dq, dk, dv, batch, heads, seq, hidden, dtype, is_causal, scale, ws,
+                              PMKL_BWD_STATIC_SCRATCH_BYTES, PMKL_ATTN_AUTO, stream);
 }
 
 size_t pmkl_causal_attention_bwd_workspace_size(int batch, int heads, int seq, int hidden, int dtype) {
