@@ -14,7 +14,8 @@ One JSON line on rank 0:
   e2e       the same metric through the public API
             (pmkl_function.fused_self_attention) with the step's inputs copied
             host->device from pinned memory and O, m, l copied back inside the
-            timed region;
+            timed region; the step's slices go in --e2e-chunks chunks whose
+            copies overlap the attention of the neighbouring chunks;
   roofline  the attention kernel's achieved TFLOP/s per launch vs the measured
             bf16 peak (MEASURED_PEAKS.json);
   cpu_baseline  the reference's own CPU implementation (its torch extension
@@ -61,6 +62,8 @@ def parse_args():
     ap.add_argument("--workload", default="attention", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="pmkl_b200", choices=["pmkl_b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="slice chunks per end-to-end step (copies of one chunk overlap the attention of another)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
@@ -410,23 +413,43 @@ def run_attention(args, wl, rank, world, local):
     achieved_min = max_over_ranks(-achieved, world)  # slowest rank
     peaks = measured_peaks()
 
-    # End to end through the public API: H2D of q, k, v from pinned memory,
-    # the fused_self_attention call, D2H of O, m, l, every step.
+    # End to end through the public API: every step copies q, k, v in from
+    # pinned host memory, calls fused_self_attention and copies O, m, l back.
+    # The step's slices go in chunks on three streams, so that the H2D copy of
+    # chunk c+1, the attention of chunk c and the D2H copy of chunk c-1 overlap
+    # (PCIe carries both directions at once).
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
     oh = torch.empty(q.shape, dtype=dt).pin_memory()
     mh = torch.empty(m.shape, dtype=dt).pin_memory()
     lh = torch.empty(m.shape, dtype=dt).pin_memory()
     qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    shp = (ns, 1, S, D)
+    n_chunks = max(1, min(args.e2e_chunks, ns))
+    bounds = [shard(ns, n_chunks, c) for c in range(n_chunks)]
+    s_in, s_run, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
+    ev_run = [torch.cuda.Event() for _ in range(n_chunks)]
 
     def e2e_step():
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        out, om, ol = fused_self_attention(qd.view(shp), kd.view(shp), vd.view(shp), causal)
-        oh.copy_(out, non_blocking=True)
-        mh.copy_(om, non_blocking=True)
-        lh.copy_(ol, non_blocking=True)
+        main = torch.cuda.current_stream()
+        s_in.wait_stream(main)
+        for c, (a, b) in enumerate(bounds):
+            with torch.cuda.stream(s_in):
+                qd[a:b].copy_(qh[a:b], non_blocking=True)
+                kd[a:b].copy_(kh[a:b], non_blocking=True)
+                vd[a:b].copy_(vh[a:b], non_blocking=True)
+                ev_in[c].record(s_in)
+            with torch.cuda.stream(s_run):
+                s_run.wait_event(ev_in[c])
+                out, om, ol = fused_self_attention(qd[a:b], kd[a:b], vd[a:b], causal)
+                ev_run[c].record(s_run)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_run[c])
+                for src in (out, om, ol):
+                    src.record_stream(s_out)
+                oh[a:b].copy_(out, non_blocking=True)
+                mh[a:b].copy_(om, non_blocking=True)
+                lh[a:b].copy_(ol, non_blocking=True)
+        main.wait_stream(s_out)
 
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
     e2e_ms, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
@@ -455,7 +478,8 @@ def run_attention(args, wl, rank, world, local):
         "per_gpu_tflops": value / world,
         "frac_of_peak": value / world / peaks["bf16_tflops"],
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "pmkl_function.fused_self_attention", "steps": e2e_steps},
+                "api": "pmkl_function.fused_self_attention", "steps": e2e_steps,
+                "chunks": n_chunks, "overlap": "H2D / attention / D2H of consecutive chunks on three streams"},
         "gpu_launches": args.steps,
         "roofline": {"bound": "tensor", "achieved": -achieved_min, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": -achieved_min / peaks["bf16_tflops"],
@@ -516,13 +540,32 @@ def run_attention_bwd(args, wl, rank, world, local):
     hosts = [t.cpu().pin_memory() for t in (do, q, k, v, m, l)]
     devs = [torch.empty_like(t) for t in (do, q, k, v, m, l)]
     outs_h = [torch.empty(q.shape, dtype=dt).pin_memory() for _ in range(3)]
+    n_chunks = max(1, min(args.e2e_chunks, ns))
+    bounds = [shard(ns, n_chunks, c) for c in range(n_chunks)]
+    s_in, s_run, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
+    ev_run = [torch.cuda.Event() for _ in range(n_chunks)]
 
     def e2e_step():
-        for d_, h_ in zip(devs, hosts):
-            d_.copy_(h_, non_blocking=True)
-        grads = pmkl_pytorch_ext.fused_self_attention_bw(*devs, causal)
-        for h_, g_ in zip(outs_h, grads):
-            h_.copy_(g_, non_blocking=True)
+        # Slice chunks on three streams: H2D of chunk c+1, backward of chunk c
+        # and D2H of chunk c-1 overlap.
+        main = torch.cuda.current_stream()
+        s_in.wait_stream(main)
+        for c, (a, b) in enumerate(bounds):
+            with torch.cuda.stream(s_in):
+                for d_, h_ in zip(devs, hosts):
+                    d_[a:b].copy_(h_[a:b], non_blocking=True)
+                ev_in[c].record(s_in)
+            with torch.cuda.stream(s_run):
+                s_run.wait_event(ev_in[c])
+                grads = pmkl_pytorch_ext.fused_self_attention_bw(*(d_[a:b] for d_ in devs), causal)
+                ev_run[c].record(s_run)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_run[c])
+                for h_, g_ in zip(outs_h, grads):
+                    g_.record_stream(s_out)
+                    h_[a:b].copy_(g_, non_blocking=True)
+        main.wait_stream(s_out)
 
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
     e2e_ms, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
@@ -553,7 +596,8 @@ def run_attention_bwd(args, wl, rank, world, local):
         "per_gpu_tflops": value / world,
         "frac_of_peak": value / world / peaks["bf16_tflops"],
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "pmkl_pytorch_ext.fused_self_attention_bw", "steps": e2e_steps},
+                "api": "pmkl_pytorch_ext.fused_self_attention_bw", "steps": e2e_steps,
+                "chunks": n_chunks, "overlap": "H2D / backward / D2H of consecutive chunks on three streams"},
         "gpu_launches": 4 * args.steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"],
@@ -598,11 +642,28 @@ def run_softmax(args, wl, rank, world, local):
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
     xd, yd = torch.empty_like(x), torch.empty_like(y)
+    n_chunks = max(1, min(args.e2e_chunks, rows))
+    bounds = [shard(rows, n_chunks, c) for c in range(n_chunks)]
+    s_in, s_run, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
+    ev_run = [torch.cuda.Event() for _ in range(n_chunks)]
 
     def e2e_step():
-        xd.copy_(xh, non_blocking=True)
-        pmkl_b200.warp_softmax_fwd(yd, xd, el, el, rows, stream=stream)
-        yh.copy_(yd, non_blocking=True)
+        # Row chunks on three streams: H2D of chunk c+1, softmax of chunk c and
+        # D2H of chunk c-1 overlap.
+        main = torch.cuda.current_stream()
+        s_in.wait_stream(main)
+        for c, (a, b) in enumerate(bounds):
+            with torch.cuda.stream(s_in):
+                xd[a:b].copy_(xh[a:b], non_blocking=True)
+                ev_in[c].record(s_in)
+            s_run.wait_event(ev_in[c])
+            pmkl_b200.warp_softmax_fwd(yd[a:b], xd[a:b], el, el, b - a, stream=s_run)
+            ev_run[c].record(s_run)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_run[c])
+                yh[a:b].copy_(yd[a:b], non_blocking=True)
+        main.wait_stream(s_out)
 
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
     e2e_ms, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
@@ -625,7 +686,8 @@ def run_softmax(args, wl, rank, world, local):
         "config": {"workload": wl[7], "rows": rows_all, "elements": el, "parallelism": f"row shards over {world} GPU(s)",
                    "l2": "256 MiB in + 256 MiB out per GPU at N=1 exceed the 126 MB L2; no flush"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": rows * el * 4,
-                "d2h_bytes_per_step": rows * el * 4, "api": "pmkl_warp_softmax_fwd (C ABI)", "steps": e2e_steps},
+                "d2h_bytes_per_step": rows * el * 4, "api": "pmkl_warp_softmax_fwd (C ABI)", "steps": e2e_steps,
+                "chunks": n_chunks, "overlap": "H2D / softmax / D2H of consecutive row chunks on three streams"},
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} copy bandwidth",
