@@ -92,6 +92,34 @@ int pmkl_causal_attention_fwd_ex(const void *q, const void *k, const void *v, vo
                                  int batch, int heads, int seq, int hidden, int dtype, int out_dtype,
                                  int is_causal, float scale, int kernel, void *stream);
 
+/*
+ * As pmkl_causal_attention_fwd_ex for strided and grouped-query inputs, so that
+ * callers with other layouts (e.g. [batch, seq, heads, hidden] views, or K/V
+ * with fewer heads) need no copy; the reference makes its inputs contiguous
+ * (fused_self_attention.cpp:160-162) and takes equal head counts only (:141).
+ *
+ *   q, o       : [batch, heads, seq, hidden] elements at
+ *                b * s[0] + h * s[1] + row * s[2] + col (s = q_strides /
+ *                o_strides, element strides; the hidden dimension is
+ *                contiguous).
+ *   k, v       : the same with kv_heads heads (k_strides / v_strides); query
+ *                head h reads K/V head h / (heads / kv_heads).  kv_heads must
+ *                divide heads (kv_heads == heads: ordinary attention; 1:
+ *                multi-query).
+ *   m, l       : contiguous [batch, heads, seq], as in the forward.
+ *   a NULL strides pointer means that tensor is contiguous.
+ * The tensor-core kernel runs when the pointers are 16-byte aligned and every
+ * stride is a multiple of 16 bytes (fp32 o: of 4 elements); otherwise the
+ * CUDA-core kernel.  Negative strides and a kv_heads that does not divide heads
+ * give PMKL_ERR_INVALID_SHAPE.  PMKL_ATTN_TCGEN05_SIMPLE accepts contiguous,
+ * equal-head inputs only.
+ */
+int pmkl_causal_attention_fwd_strided(const void *q, const void *k, const void *v, void *o, void *m, void *l,
+                                      int batch, int heads, int kv_heads, int seq, int hidden,
+                                      const int64_t *q_strides, const int64_t *k_strides, const int64_t *v_strides,
+                                      const int64_t *o_strides, int dtype, int out_dtype, int is_causal, float scale,
+                                      int kernel, void *stream);
+
 /* The kernel pmkl_causal_attention_fwd_ex would run for these arguments:
  * PMKL_ATTN_TCGEN05 (the persistent two-tile tensor-core kernel),
  * PMKL_ATTN_TCGEN05_SIMPLE, PMKL_ATTN_SIMT, or a negative pmkl_status.  Needs

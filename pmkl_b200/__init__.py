@@ -59,6 +59,9 @@ def capi() -> ctypes.CDLL:
         L.pmkl_causal_attention_fwd.argtypes = [vp] * 6 + [i32] * 7 + [f32, vp]
         L.pmkl_causal_attention_fwd_ex.restype = i32
         L.pmkl_causal_attention_fwd_ex.argtypes = [vp] * 6 + [i32] * 7 + [f32, i32, vp]
+        i64p = ctypes.POINTER(ctypes.c_int64)
+        L.pmkl_causal_attention_fwd_strided.restype = i32
+        L.pmkl_causal_attention_fwd_strided.argtypes = [vp] * 6 + [i32] * 5 + [i64p] * 4 + [i32] * 3 + [f32, i32, vp]
         L.pmkl_causal_attention_bwd.restype = i32
         L.pmkl_causal_attention_bwd.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp, ctypes.c_size_t, vp]
         L.pmkl_causal_attention_bwd_ex.restype = i32
@@ -109,6 +112,26 @@ def attention_fwd(q, k, v, o, m, l, is_causal: bool, scale: float = 0.0, kernel:
         int(kernel), _stream_ptr(stream))
     if rc != PMKL_OK:
         raise PmklError(rc, "pmkl_causal_attention_fwd")
+
+
+def attention_fwd_strided(q, k, v, o, m, l, is_causal: bool, scale: float = 0.0, kernel: int = KERNEL_AUTO,
+                          stream=None) -> None:
+    """pmkl_causal_attention_fwd_strided on torch CUDA tensors of logical shape
+    [B, H, S, D] (q, o) and [B, H_kv, S, D] (k, v) with any strides whose last
+    dimension is contiguous; m, l contiguous [B, H, S]."""
+    B, H, S, D = q.shape
+    Hkv = k.shape[1]
+
+    def st(t):
+        assert t.stride(3) == 1, "the hidden dimension must be contiguous"
+        return (ctypes.c_int64 * 3)(t.stride(0), t.stride(1), t.stride(2))
+
+    rc = capi().pmkl_causal_attention_fwd_strided(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), m.data_ptr(), l.data_ptr(), B, H, Hkv, S, D,
+        st(q), st(k), st(v), st(o), torch_dtype_code(q.dtype), torch_dtype_code(o.dtype), int(bool(is_causal)),
+        float(scale), int(kernel), _stream_ptr(stream))
+    if rc != PMKL_OK:
+        raise PmklError(rc, "pmkl_causal_attention_fwd_strided")
 
 
 def attention_bwd_workspace_size(B: int, H: int, S: int, D: int, dtype) -> int:

@@ -73,6 +73,9 @@ struct Cfg {
 struct Params {
     int S;
     int BH;
+    int H;         // query heads per batch entry (slice bh = b * H + h)
+    int kv_group;  // query heads per K/V head: slice (b, h) reads K/V head h / kv_group
+    long long o_sb, o_sh, o_ss;  // element strides of O (batch, head, row) for fp32 output
     int n_pairs;     // ceil(n_qt / 2)
     int n_units;     // n_pairs * BH
     int group;       // (b, h) slices per scheduling group
@@ -264,13 +267,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
                 const Unit w = decode(p, u);
+                const int bb = w.bh / p.H;
+                const int hh = w.bh - bb * p.H;
+                const int hkv = hh / p.kv_group;
                 for (int x = 0; x < 2 && ok; ++x) {
                     if (!w.act[x]) continue;
                     if (qc[x] > 0 && !(ok = mbar_wait(&q_empty[x], (qc[x] - 1) & 1, abort_flag))) break;
                     mbar_arrive_expect_tx(&q_full[x], TILE);
                     for (int b = 0; b < C::kBoxes; ++b)
-                        tma_load_3d(sQ + x * TILE + b * kBoxBytes, &tm_q, &q_full[x], b * kBoxCols, w.row0 + 128 * x,
-                                    w.bh);
+                        tma_load_4d(sQ + x * TILE + b * kBoxBytes, &tm_q, &q_full[x], b * kBoxCols, w.row0 + 128 * x,
+                                    hh, bb);
                     ++qc[x];
                 }
                 for (int j = 0; ok && j < w.n_max; ++j) {
@@ -280,7 +286,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mbar_arrive_expect_tx(&kv_full[s], TILE);
                         const CUtensorMap *map = kv ? &tm_v : &tm_k;
                         for (int b = 0; b < C::kBoxes; ++b)
-                            tma_load_3d(sRing + s * TILE + b * kBoxBytes, map, &kv_full[s], b * kBoxCols, j * 128, w.bh);
+                            tma_load_4d(sRing + s * TILE + b * kBoxBytes, map, &kv_full[s], b * kBoxCols, j * 128, hkv,
+                                        bb);
                         ++kvc;
                     }
                 }
@@ -521,8 +528,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float inv_l = 1.f / l;
                     const int row = w.row0 + 128 * x + r_local;
                     const uint32_t oa = lane_base + col_o(x);
+                    const int bb = w.bh / p.H;
+                    const int hh = w.bh - bb * p.H;
                     if (p.out_dtype == PMKL_DTYPE_F32) {
-                        float *orow = static_cast<float *>(p.o_f32) + (static_cast<size_t>(w.bh) * p.S + row) * D;
+                        float *orow = static_cast<float *>(p.o_f32) + bb * p.o_sb + hh * p.o_sh + row * p.o_ss;
 #pragma unroll
                         for (int cc = 0; cc < D / 32; ++cc) {
                             uint32_t o[32];
@@ -577,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 // Once all four warps have written their rows of this box,
                                 // store it and hand the buffer back when the store has read it.
                                 if ((ok = mbar_wait(stg_written, nb & 1, abort_flag))) {
-                                    tma_store_3d(&tm_o, sStage, b * kBoxCols, w.row0 + 128 * x, w.bh);
+                                    tma_store_4d(&tm_o, sStage, b * kBoxCols, w.row0 + 128 * x, hh, bb);
                                     tma_store_commit();
                                     tma_store_wait_read0();
                                 }

@@ -54,7 +54,7 @@ template <typename T, int DMAX>
 __global__ void __launch_bounds__(kThreads)
     attn_fwd_simt_kernel(const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v, void *__restrict__ o,
                          void *__restrict__ m_out, void *__restrict__ l_out, int S, int D, int BH, int n_qt, int causal,
-                         float scale, int out_dtype) {
+                         float scale, int out_dtype, const AttnLayout lay) {
     extern __shared__ float smem_f[];
     float *Qs = smem_f;                      // [kBM][DMAX]
     float *Ks = Qs + kBM * DMAX;             // [kBN][DMAX + 1]
@@ -67,13 +67,17 @@ __global__ void __launch_bounds__(kThreads)
     const int bid = blockIdx.x;
     const int qt = causal ? (n_qt - 1 - bid / BH) : (bid / BH);
     const int bh = bid % BH;
-    const size_t base = static_cast<size_t>(bh) * S * D;
+    const int bb = bh / lay.H, hh = bh % lay.H, hk = hh / lay.kv_group;
+    const long long qb = bb * lay.q[0] + hh * lay.q[1];
+    const long long kb0 = bb * lay.k[0] + hk * lay.k[1];
+    const long long vb0 = bb * lay.v[0] + hk * lay.v[1];
+    const long long ob0 = bb * lay.o[0] + hh * lay.o[1];
     const int row0 = qt * kBM;
 
     for (int idx = threadIdx.x; idx < kBM * DMAX; idx += kThreads) {
         const int r = idx / DMAX, d = idx % DMAX;
         const int row = row0 + r;
-        Qs[idx] = (row < S && d < D) ? ld_f(q + base + static_cast<size_t>(row) * D + d) : 0.f;
+        Qs[idx] = (row < S && d < D) ? ld_f(q + qb + row * lay.q[2] + d) : 0.f;
     }
 
     float mrow[kRowsPerWarp], lrow[kRowsPerWarp], acc[kRowsPerWarp][CPL];
@@ -92,9 +96,8 @@ __global__ void __launch_bounds__(kThreads)
             const int r = idx / DMAX, d = idx % DMAX;
             const int key = kb + r;
             const bool in = key < S && d < D;
-            const size_t g = base + static_cast<size_t>(key) * D + d;
-            Ks[r * KS + d] = in ? ld_f(k + g) : 0.f;
-            Vs[idx] = in ? ld_f(v + g) : 0.f;
+            Ks[r * KS + d] = in ? ld_f(k + kb0 + key * lay.k[2] + d) : 0.f;
+            Vs[idx] = in ? ld_f(v + vb0 + key * lay.v[2] + d) : 0.f;
         }
         __syncthreads();
 
@@ -134,7 +137,7 @@ __global__ void __launch_bounds__(kThreads)
         const int row = row0 + warp * kRowsPerWarp + i;
         if (row >= S) continue;
         const float inv = 1.f / lrow[i];
-        const size_t ob = base + static_cast<size_t>(row) * D;
+        const long long ob = ob0 + row * lay.o[2];
 #pragma unroll
         for (int t = 0; t < CPL; ++t) {
             const int d = lane + 32 * t;

@@ -45,6 +45,16 @@ struct Elem<__nv_bfloat16> {
     __device__ __forceinline__ static __nv_bfloat16 from_float(float v) { return __float2bfloat16_rn(v); }
 };
 
+// Element strides of the attention tensors.  q, k, v, o are [batch][head]
+// [row][head_size] with the head-size dimension contiguous; k and v have
+// H / kv_group heads, query head h reading K/V head h / kv_group.  m and l
+// are always contiguous [batch * H][rows].
+struct AttnLayout {
+    int H;
+    int kv_group;
+    long long q[3], k[3], v[3], o[3];  // (batch, head, row)
+};
+
 // Stores one fp32 value as out_dtype.
 __device__ __forceinline__ void store_as(void *base, size_t idx, int out_dtype, float v) {
     if (out_dtype == PMKL_DTYPE_F32)

@@ -115,7 +115,47 @@ bool make_tile_map(CUtensorMap *map, const void *base, int dtype, int cols, int 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [batch][heads][rows][cols] 16-bit tensor with element strides st = (batch,
+// head, row) and contiguous columns, viewed as 4-D {cols, rows, heads, batch}
+// for 128-row x 64-column boxes with the 128-byte swizzle.  A dimension of
+// extent 1 is never stepped, so its stride is replaced by a valid one.
+bool make_tile_map_4d(CUtensorMap *map, const void *base, int dtype, int cols, int rows, int heads, int batch,
+                      const long long (&st)[3]) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const CUtensorMapDataType dt =
+        dtype == PMKL_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint64_t row_b = static_cast<cuuint64_t>(st[2]) * 2;
+    const cuuint64_t head_b = heads > 1 ? static_cast<cuuint64_t>(st[1]) * 2 : row_b * static_cast<cuuint64_t>(rows);
+    const cuuint64_t batch_b =
+        batch > 1 ? static_cast<cuuint64_t>(st[0]) * 2 : head_b * static_cast<cuuint64_t>(heads);
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[3] = {row_b, head_b, batch_b};
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(tc::kBoxCols), 128u, 1u, 1u};
+    const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+    return enc(map, dt, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+AttnLayout contiguous_layout(int H, int S, int D) {
+    AttnLayout L;
+    L.H = H;
+    L.kv_group = 1;
+    const long long s3[3] = {static_cast<long long>(H) * S * D, static_cast<long long>(S) * D, D};
+    for (int i = 0; i < 3; ++i) L.q[i] = L.k[i] = L.v[i] = L.o[i] = s3[i];
+    return L;
+}
+
+bool layout_contiguous(const AttnLayout &L, int S, int D) {
+    const AttnLayout c = contiguous_layout(L.H, S, D);
+    for (int i = 0; i < 3; ++i)
+        if (L.q[i] != c.q[i] || L.k[i] != c.k[i] || L.v[i] != c.v[i] || L.o[i] != c.o[i]) return false;
+    return L.kv_group == 1;
+}
 
 // ------------------------------------------------------------------ attention launchers
 template <int D, bool BF16>
@@ -176,19 +216,27 @@ bool pp_launchable() {
 
 template <int D, bool BF16>
 int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int BH, int causal,
-              float scale, int dtype, int out_dtype, cudaStream_t stream) {
+              float scale, int dtype, int out_dtype, const AttnLayout &lay, cudaStream_t stream) {
     using C = pp::Cfg<D>;
     static std::once_flag smem_once[kMaxDevices];
     auto kernel = pp::attn_fwd_pp_kernel<D, BF16>;
     if (!ensure_smem(kernel, C::kSmemBytes, smem_once)) return PMKL_ERR_LAUNCH;
     CUtensorMap tq, tk, tv, to;
     const bool o16 = out_dtype != PMKL_DTYPE_F32;
-    if (!make_tile_map(&tq, q, dtype, D, S, BH) || !make_tile_map(&tk, k, dtype, D, S, BH) ||
-        !make_tile_map(&tv, v, dtype, D, S, BH) || !make_tile_map(&to, o16 ? o : q, dtype, D, S, BH))
+    const int B = BH / lay.H, Hkv = lay.H / lay.kv_group;
+    if (!make_tile_map_4d(&tq, q, dtype, D, S, lay.H, B, lay.q) ||
+        !make_tile_map_4d(&tk, k, dtype, D, S, Hkv, B, lay.k) ||
+        !make_tile_map_4d(&tv, v, dtype, D, S, Hkv, B, lay.v) ||
+        !make_tile_map_4d(&to, o16 ? o : q, dtype, D, S, lay.H, B, o16 ? lay.o : lay.q))
         return PMKL_ERR_LAUNCH;
     pp::Params p;
     p.S = S;
     p.BH = BH;
+    p.H = lay.H;
+    p.kv_group = lay.kv_group;
+    p.o_sb = lay.o[0];
+    p.o_sh = lay.o[1];
+    p.o_ss = lay.o[2];
     const int n_qt = (S + 127) / 128;
     p.n_pairs = (n_qt + 1) / 2;
     const long long units = static_cast<long long>(p.n_pairs) * BH;
@@ -215,7 +263,7 @@ int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, voi
 
 template <typename T, int DMAX>
 int launch_simt_t(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int D, int BH,
-                  int causal, float scale, int out_dtype, cudaStream_t stream) {
+                  int causal, float scale, int out_dtype, const AttnLayout &lay, cudaStream_t stream) {
     static std::once_flag smem_once[kMaxDevices];
     auto kernel = simt::attn_fwd_simt_kernel<T, DMAX>;
     constexpr int smem = simt::smem_bytes<DMAX>();
@@ -225,45 +273,61 @@ int launch_simt_t(const void *q, const void *k, const void *v, void *o, void *m,
     if (blocks > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
     kernel<<<static_cast<unsigned>(blocks), simt::kThreads, smem, stream>>>(
         static_cast<const T *>(q), static_cast<const T *>(k), static_cast<const T *>(v), o, m, l, S, D, BH, n_qt,
-        causal, scale, out_dtype);
+        causal, scale, out_dtype, lay);
     return launch_status();
 }
 
 template <typename T>
 int launch_simt(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int D, int BH,
-                int causal, float scale, int out_dtype, cudaStream_t stream) {
-    if (D <= 32) return launch_simt_t<T, 32>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
-    if (D <= 64) return launch_simt_t<T, 64>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
-    if (D <= 128) return launch_simt_t<T, 128>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
-    return launch_simt_t<T, 256>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, stream);
+                int causal, float scale, int out_dtype, const AttnLayout &lay, cudaStream_t stream) {
+    if (D <= 32) return launch_simt_t<T, 32>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, lay, stream);
+    if (D <= 64) return launch_simt_t<T, 64>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, lay, stream);
+    if (D <= 128) return launch_simt_t<T, 128>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, lay, stream);
+    return launch_simt_t<T, 256>(q, k, v, o, m, l, S, D, BH, causal, scale, out_dtype, lay, stream);
 }
 
-bool tc_applies(const void *q, const void *k, const void *v, const void *o, int D, int dtype, int out_dtype) {
+// The tensor-core kernels read q, k, v (and write a 16-bit o) through TMA:
+// 16-byte aligned bases and strides that are multiples of 16 bytes; an fp32 o
+// is written with 16-byte vector stores.
+bool strides_ok(const long long (&s)[3], int elems_per_16b) {
+    for (long long x : s)
+        if (x < 0 || x % elems_per_16b != 0 || x >= (1LL << 38)) return false;
+    return true;
+}
+
+bool tc_applies(const void *q, const void *k, const void *v, const void *o, int D, int dtype, int out_dtype,
+                const AttnLayout &lay) {
     if (dtype != PMKL_DTYPE_F16 && dtype != PMKL_DTYPE_BF16) return false;
     if (D != 64 && D != 128) return false;
     if (out_dtype != dtype && out_dtype != PMKL_DTYPE_F32) return false;
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return false;
+    if (!strides_ok(lay.q, 8) || !strides_ok(lay.k, 8) || !strides_ok(lay.v, 8)) return false;
+    if (!strides_ok(lay.o, out_dtype == PMKL_DTYPE_F32 ? 4 : 8)) return false;
     return true;
 }
 
 // Which kernel runs: the persistent tensor-core kernel when it applies (and
 // its register split is available), the one-tile tensor-core kernel when
 // asked for or as the fallback, else the CUDA-core kernel.
-int select_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype, int out_dtype,
-                  int kernel) {
-    const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype);
-    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+int select_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int S, int dtype,
+                  int out_dtype, int kernel, const AttnLayout &lay) {
+    const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype, lay);
+    // The one-tile kernel reads contiguous [B*H, S, D] tensors only.
+    const bool simple_ok = tc_ok && layout_contiguous(lay, S, hidden);
+    if (kernel == PMKL_ATTN_TCGEN05 && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if (kernel == PMKL_ATTN_TCGEN05_SIMPLE && !simple_ok) return PMKL_ERR_UNSUPPORTED;
     if (kernel == PMKL_ATTN_SIMT || !tc_ok) return PMKL_ATTN_SIMT;
     if (kernel == PMKL_ATTN_TCGEN05_SIMPLE) return PMKL_ATTN_TCGEN05_SIMPLE;
     const bool bf = dtype == PMKL_DTYPE_BF16;
     const bool ready = hidden == 64 ? (bf ? pp_launchable<64, true>() : pp_launchable<64, false>())
                                     : (bf ? pp_launchable<128, true>() : pp_launchable<128, false>());
-    return ready ? PMKL_ATTN_TCGEN05 : PMKL_ATTN_TCGEN05_SIMPLE;
+    if (ready) return PMKL_ATTN_TCGEN05;
+    return simple_ok ? PMKL_ATTN_TCGEN05_SIMPLE : PMKL_ATTN_SIMT;
 }
 
 int attention_impl(const void *q, const void *k, const void *v, void *o, void *m, void *l, int batch, int heads,
                    int seq, int hidden, int dtype, int out_dtype, int is_causal, float scale, int kernel,
-                   void *stream_) {
+                   void *stream_, const AttnLayout *layout = nullptr) {
     if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
     if (out_dtype != dtype && out_dtype != PMKL_DTYPE_F32) return PMKL_ERR_INVALID_DTYPE;
@@ -280,15 +344,18 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     const float sc = (scale > 0.f) ? scale : 1.0f / sqrtf(static_cast<float>(hidden));
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     const int causal = is_causal ? 1 : 0;
-    const int chosen = select_kernel(q, k, v, o, hidden, dtype, out_dtype, kernel);
+    const AttnLayout lay = layout ? *layout : contiguous_layout(heads, seq, hidden);
+    const int chosen = select_kernel(q, k, v, o, hidden, seq, dtype, out_dtype, kernel, lay);
     if (chosen < 0) return chosen;
     if (chosen == PMKL_ATTN_TCGEN05) {
         const int bh = static_cast<int>(BH);
         if (dtype == PMKL_DTYPE_BF16)
-            return hidden == 64 ? launch_pp<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
-                                : launch_pp<128, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
-        return hidden == 64 ? launch_pp<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream)
-                            : launch_pp<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, stream);
+            return hidden == 64
+                       ? launch_pp<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream)
+                       : launch_pp<128, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream);
+        return hidden == 64
+                   ? launch_pp<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream)
+                   : launch_pp<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream);
     }
     if (chosen == PMKL_ATTN_TCGEN05_SIMPLE) {
         const int bh = static_cast<int>(BH);
@@ -300,10 +367,10 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     }
     const int bh = static_cast<int>(BH);
     if (dtype == PMKL_DTYPE_F32)
-        return launch_simt<float>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, stream);
+        return launch_simt<float>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, lay, stream);
     if (dtype == PMKL_DTYPE_F16)
-        return launch_simt<__half>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, stream);
-    return launch_simt<__nv_bfloat16>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, stream);
+        return launch_simt<__half>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, lay, stream);
+    return launch_simt<__nv_bfloat16>(q, k, v, o, m, l, seq, hidden, bh, causal, sc, out_dtype, lay, stream);
 }
 
 // ------------------------------------------------------------------ backward
@@ -634,6 +701,35 @@ size_t pmkl_causal_attention_bwd_workspace_size(int batch, int heads, int seq, i
     return bwd_workspace_size(static_cast<long long>(batch) * heads, seq, hidden, dtype);
 }
 
+int pmkl_causal_attention_fwd_strided(const void *q, const void *k, const void *v, void *o, void *m, void *l,
+                                      int batch, int heads, int kv_heads, int seq, int hidden,
+                                      const int64_t *q_strides, const int64_t *k_strides, const int64_t *v_strides,
+                                      const int64_t *o_strides, int dtype, int out_dtype, int is_causal, float scale,
+                                      int kernel, void *stream) {
+    if (batch < 0 || heads < 0 || seq < 0 || hidden < 0 || kv_heads < 0) return PMKL_ERR_INVALID_SHAPE;
+    if (heads > 0 && (kv_heads == 0 || heads % kv_heads != 0)) return PMKL_ERR_INVALID_SHAPE;
+    AttnLayout lay = contiguous_layout(heads > 0 ? heads : 1, seq, hidden);
+    lay.kv_group = (heads > 0 && kv_heads > 0) ? heads / kv_heads : 1;
+    const long long Hkv = kv_heads > 0 ? kv_heads : 1;
+    const long long kv_contig[3] = {Hkv * seq * hidden, static_cast<long long>(seq) * hidden, hidden};
+    const int64_t *given[4] = {q_strides, k_strides, v_strides, o_strides};
+    long long *dst[4] = {lay.q, lay.k, lay.v, lay.o};
+    for (int t = 0; t < 4; ++t) {
+        const long long extent[3] = {batch, (t == 1 || t == 2) ? Hkv : heads, seq};
+        for (int i = 0; i < 3; ++i) {
+            if (given[t]) {
+                if (given[t][i] < 0) return PMKL_ERR_INVALID_SHAPE;
+                // A dimension of extent 1 is never stepped: its stride does not matter.
+                dst[t][i] = extent[i] == 1 ? 0 : given[t][i];
+            } else if (t == 1 || t == 2) {
+                dst[t][i] = kv_contig[i];
+            }
+        }
+    }
+    return attention_impl(q, k, v, o, m, l, batch, heads, seq, hidden, dtype, out_dtype, is_causal, scale, kernel,
+                          stream, &lay);
+}
+
 int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
                                    int out_dtype, int kernel) {
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
@@ -642,7 +738,8 @@ int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, 
         return PMKL_ERR_UNSUPPORTED;
     const int dev_rc = current_device_ok();
     if (dev_rc != PMKL_OK) return dev_rc;
-    return select_kernel(q, k, v, o, hidden, dtype, out_dtype, kernel);
+    const AttnLayout lay = contiguous_layout(1, 128, hidden > 0 ? hidden : 1);
+    return select_kernel(q, k, v, o, hidden, 128, dtype, out_dtype, kernel, lay);
 }
 
 int pmkl_warp_softmax_fwd(void *dst, const void *src, int elements, int stride, int rows, int in_dtype,

@@ -115,6 +115,24 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+// 4-D forms: coordinates (x, y, z, w) = (column, row, head, batch).
+__device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int x, int y,
+                                            int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *smem_src, int x, int y, int z,
+                                             int w) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z), "r"(w)
+                 : "memory");
+}
+
 // Contiguous global -> shared copy of `bytes` (a multiple of 16; both
 // addresses 16-byte aligned) into this CTA's shared memory, completion
 // signalled on `bar` as transaction bytes.

@@ -27,10 +27,17 @@ int pmkl_dtype_of(at::ScalarType t) {
     }
 }
 
-void check_inputs(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v) {
+void check_inputs(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v, bool allow_kv_heads = false) {
     // fused_self_attention.cpp:140-141
     TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "Input tensor shapes must match");
-    TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(), "Input tensor shapes must match");
+    if (allow_kv_heads) {
+        // Grouped-query form (no reference counterpart): k and v may have fewer heads.
+        TORCH_CHECK(k.sizes() == v.sizes() && k.size(0) == q.size(0) && k.size(2) == q.size(2) &&
+                        k.size(3) == q.size(3) && k.size(1) > 0 && q.size(1) % k.size(1) == 0,
+                    "Input tensor shapes must match (k and v may have heads dividing q's heads)");
+    } else {
+        TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(), "Input tensor shapes must match");
+    }
     TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(),
                 "pmkl_pytorch_ext (B200 build) runs on CUDA tensors only; got a CPU tensor");
     TORCH_CHECK(q.device() == k.device() && q.device() == v.device(), "q, k and v must be on the same device");
@@ -44,25 +51,34 @@ void check_inputs(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v)
 
 std::tuple<at::Tensor, at::Tensor, at::Tensor> forward_impl(const at::Tensor &q, const at::Tensor &k,
                                                             const at::Tensor &v, bool is_causal, bool out_fp32,
-                                                            int64_t kernel, double scale) {
-    check_inputs(q, k, v);
+                                                            int64_t kernel, double scale, bool allow_kv_heads) {
+    check_inputs(q, k, v, allow_kv_heads);
     const c10::cuda::CUDAGuard guard(q.device());
     const int B = static_cast<int>(q.size(0)), H = static_cast<int>(q.size(1));
     const int S = static_cast<int>(q.size(2)), D = static_cast<int>(q.size(3));
-    // fused_self_attention.cpp:160-162 makes the inputs contiguous.
-    const at::Tensor qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
+    const int Hkv = static_cast<int>(k.size(1));
+    // The reference makes the inputs contiguous (fused_self_attention.cpp:160-162);
+    // here they are read in place through their strides, and copied only when
+    // the hidden dimension itself is strided.
+    const auto rows_ok = [](const at::Tensor &t) { return t.size(3) <= 1 || t.stride(3) == 1; };
+    const at::Tensor qc = rows_ok(q) ? q : q.contiguous();
+    const at::Tensor kc = rows_ok(k) ? k : k.contiguous();
+    const at::Tensor vc = rows_ok(v) ? v : v.contiguous();
+    const int64_t qs[3] = {qc.stride(0), qc.stride(1), qc.stride(2)};
+    const int64_t ks[3] = {kc.stride(0), kc.stride(1), kc.stride(2)};
+    const int64_t vs[3] = {vc.stride(0), vc.stride(1), vc.stride(2)};
     // Outputs in v's dtype (fused_self_attention.cpp:148-150), contiguous.
     const auto opts = out_fp32 ? v.options().dtype(at::kFloat) : v.options();
-    at::Tensor out = at::empty(v.sizes(), opts);
+    at::Tensor out = at::empty(q.sizes(), opts);
     at::Tensor out_m = at::empty({q.size(0), q.size(1), q.size(2)}, opts);
     at::Tensor out_l = at::empty({q.size(0), q.size(1), q.size(2)}, opts);
     const int dt = pmkl_dtype_of(v.scalar_type());
     const int odt = out_fp32 ? PMKL_DTYPE_F32 : dt;
     cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
-    const int rc = pmkl_causal_attention_fwd_ex(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(),
-                                                out_m.data_ptr(), out_l.data_ptr(), B, H, S, D, dt, odt,
-                                                is_causal ? 1 : 0, static_cast<float>(scale),
-                                                static_cast<int>(kernel), stream);
+    const int rc = pmkl_causal_attention_fwd_strided(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(),
+                                                     out_m.data_ptr(), out_l.data_ptr(), B, H, Hkv, S, D, qs, ks, vs,
+                                                     nullptr, dt, odt, is_causal ? 1 : 0, static_cast<float>(scale),
+                                                     static_cast<int>(kernel), stream);
     TORCH_CHECK(rc == PMKL_OK, "pmkl_causal_attention_fwd failed: ", pmkl_status_string(rc));
     return std::make_tuple(out, out_m, out_l);
 }
@@ -72,16 +88,17 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> forward_impl(const at::Tensor &q,
 // fused_self_attention.cpp:139 -- same name, arguments and return tuple.
 std::tuple<at::Tensor, at::Tensor, at::Tensor> fused_self_attention_fw(const at::Tensor &q, const at::Tensor &k,
                                                                        const at::Tensor &v, bool is_causal) {
-    return forward_impl(q, k, v, is_causal, false, PMKL_ATTN_AUTO, 0.0);
+    return forward_impl(q, k, v, is_causal, false, PMKL_ATTN_AUTO, 0.0, false);
 }
 
 // Extra entry (no reference counterpart): fp32 outputs, explicit kernel
-// choice and score scale, for parity tests and benchmarks.
+// choice and score scale, and k, v with fewer heads than q (grouped-query:
+// query head h reads K/V head h / (H / H_kv)).
 std::tuple<at::Tensor, at::Tensor, at::Tensor> fused_self_attention_fw_ex(const at::Tensor &q, const at::Tensor &k,
                                                                           const at::Tensor &v, bool is_causal,
                                                                           bool out_fp32, int64_t kernel,
                                                                           double scale) {
-    return forward_impl(q, k, v, is_causal, out_fp32, kernel, scale);
+    return forward_impl(q, k, v, is_causal, out_fp32, kernel, scale, true);
 }
 
 namespace {

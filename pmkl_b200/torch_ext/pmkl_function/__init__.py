@@ -13,7 +13,9 @@ Differences from the reference, all deliberate:
 * the backward runs the B200 backward kernels on CUDA tensors (the
   reference's raises ``NotImplementedError`` for any non-CPU tensor,
   ``__init__.py:27-31``).  Like the reference it ignores the gradients
-  arriving for ``out_m`` and ``out_l``.
+  arriving for ``out_m`` and ``out_l``;
+* strided q, k, v (e.g. ``[B, S, H, D]`` tensors viewed as ``[B, H, S, D]``)
+  are read in place by the forward; the backward gets contiguous copies.
 """
 import torch
 from torch.autograd import Function
@@ -41,6 +43,9 @@ class fused_self_attention_(Function):
     @staticmethod
     def backward(ctx, grad_output, grad_m, grad_l):
         q, k, v, is_casual, debug, out_m, out_l = ctx.saved_tensors
+        # The forward reads strided inputs in place; the backward kernels take
+        # contiguous ones (as the reference's does, fused_self_attention.cpp:179).
+        q, k, v = (t.contiguous() for t in (q, k, v))
         dq, dk, dv = pmkl_pytorch_ext.fused_self_attention_bw(
             grad_output, q, k, v, out_m, out_l, is_casual.item())
         return dq, dk, dv, None, None

@@ -110,6 +110,23 @@ def test_backward_workspace_size():
     assert 1.0e9 < f(16, 32, 4096, 128, 2) < 1.2e9
 
 
+def test_strided_argument_errors():
+    import ctypes
+    L = pmkl_b200.capi()
+    s = (ctypes.c_int64 * 3)(64 * 8 * 128, 128, 8 * 128)
+    neg = (ctypes.c_int64 * 3)(1, -1, 1)
+
+    def f(heads=8, kv=2, st=s, B=1, S=64):
+        return L.pmkl_causal_attention_fwd_strided(*([FAKE] * 6), B, heads, kv, S, 128, st, st, st, st, 2, 2, 1, 0.0,
+                                                   0, None)
+
+    assert f(kv=3) == -1  # kv_heads must divide heads
+    assert f(kv=0) == -1
+    assert f(kv=16) == -1
+    assert f(st=neg) == -1
+    assert f(B=0) == 0 and f(S=0) == 0  # empty problems: nothing to do
+
+
 def test_softmax_argument_errors():
     L = pmkl_b200.capi()
     f = L.pmkl_warp_softmax_fwd
