@@ -21,9 +21,10 @@
 //   3. attn_bwd_dkv_kernel: one CTA per (slice, 128-row key tile); per query
 //      tile S^T = K Q^T and dP^T = V dO^T, P^T and dS^T (16-bit) back into
 //      tensor memory, dV += P^T dO and dK += dS^T Q.
-// Both gradient kernels: warps 0-3 are the elementwise warps (one thread per
-// tensor-memory lane = tile row), warp 4 issues TMA loads, warp 5 (one
-// thread) issues tcgen05.mma.  Every wait is bounded (sm100_ptx.cuh).
+// Both gradient kernels: warps 0-7 are the elementwise warps (two per tile
+// row -- one per half of the columns; the backward's elementwise work has no
+// row reduction), warp 8 issues TMA loads, warp 9 (one thread) issues
+// tcgen05.mma.  Every wait is bounded (sm100_ptx.cuh).
 #pragma once
 
 #include "attention_tc.cuh"
@@ -34,13 +35,26 @@ namespace bwd {
 using tc::kBoxBytes;
 using tc::kBoxCols;
 
-constexpr int kThreads = 192;
-constexpr int kWarpTma = 4;
-constexpr int kWarpMma = 5;
+// Warps 0-7 are the elementwise warps: warp w serves tensor-memory lanes
+// 32 (w % 4) .. + 31 (tile rows) and the column half w / 4 (keys or queries
+// 64 (w / 4) .. + 63), so each sub-partition runs two of them.  Warp 8 issues
+// TMA loads, warp 9 (one thread) tcgen05.mma.
+constexpr int kElemWarps = 8;
+constexpr int kThreads = 32 * (kElemWarps + 2);
+constexpr int kWarpTma = kElemWarps;
+constexpr int kWarpMma = kElemWarps + 1;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;      // S or S^T (fp32); the 16-bit P / dS packed into its first 64 columns
 constexpr uint32_t kColDP = 128;   // dP or dP^T (fp32); the 16-bit dS^T packed into its first 64 columns
 constexpr uint32_t kColAcc = 256;  // dQ; or dV at kColAcc and dK at kColAcc + D
+// The elementwise warps pack their 16-bit results (P, dS) into the first half
+// of the column range they read: keys 0..63 -> columns 0..31, keys 64..127 ->
+// columns 64..95.  K-step kk (16 keys) of a product reading them from tensor
+// memory therefore starts at this column.
+__host__ __device__ constexpr uint32_t packed_col(int kk) { return (kk >> 2) * 64 + (kk & 3) * 8; }
+// The dQ kernel's second S buffer (after dQ): S(t) lives in buffer t % 2.
+template <int D>
+__host__ __device__ constexpr uint32_t col_sbuf(int b) { return b ? kColAcc + D : kColS; }
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kStatBytes = 128 * 8;  // (b, delta) of one 128-row query tile
 
@@ -170,10 +184,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&kv_empty[s], 1);
         }
         mbar_init(sd_full, 1);
-        mbar_init(p_full, 4);
+        mbar_init(p_full, kElemWarps);
         mbar_init(acc_full, 1);
         mbar_init(mma_done, 1);
-        mbar_init(staged, 4);
+        mbar_init(staged, kElemWarps);
         *abort_flag = (*reinterpret_cast<volatile unsigned int *>(&g_device_error) != 0u) ? 1 : 0;
         fence_mbarrier_init();
     }
@@ -230,51 +244,60 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t k_addr = smem_u32(sRing + 2 * s * TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(tmem + kColAcc, tmem + kColS + kk * 8, smem_desc_sw128(k_addr + kk * 2048, kBoxBytes, 1024),
-                           kIdAcc, (t > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts(tmem + kColAcc, tmem + col_sbuf<D>(t & 1) + packed_col(kk),
+                           smem_desc_sw128(k_addr + kk * 2048, kBoxBytes, 1024), kIdAcc, (t > 0 || kk > 0) ? 1u : 0u);
                 mma_commit(&kv_empty[s]);
             };
-            bool ok = mbar_wait(qd_full, 0, abort_flag);
-            for (int t = 0; ok && t < n_kv; ++t) {
+            // S(t) and dP(t) of key tile t into S buffer t % 2 and the dP buffer.
+            auto issue_sdp = [&](int t) {
                 const int s = t % NS;
-                if (!(ok = mbar_wait(&kv_full[s], (t / NS) & 1, abort_flag))) break;
-                if (t > 0) {
-                    // dS(t-1) is in tensor memory and S, dP have been read.
-                    if (!(ok = mbar_wait(p_full, (t - 1) & 1, abort_flag))) break;
-                    tc_fence_after();
-                    issue_dq(t - 1);
-                }
-                tc_fence_after();
                 const uint32_t k_addr = smem_u32(sRing + 2 * s * TILE);
                 const uint32_t v_addr = k_addr + TILE;
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                    mma_ss(tmem + kColS, smem_desc_sw128(q_addr + off, 16, 1024),
-                           smem_desc_sw128(k_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
-                }
+                const uint32_t d_s = tmem + col_sbuf<D>(t & 1);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
                     mma_ss(tmem + kColDP, smem_desc_sw128(do_addr + off, 16, 1024),
                            smem_desc_sw128(v_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
                 }
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(d_s, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+                           kIdS, kk > 0 ? 1u : 0u);
+                }
                 mma_commit(sd_full);
-            }
-            if (ok && n_kv > 0 && (ok = mbar_wait(p_full, (n_kv - 1) & 1, abort_flag))) {
+            };
+            // Per key tile t, once the elementwise warps are done with S(t), dP(t):
+            // dP(t+1) and S(t+1) first (the next elementwise pass waits on them),
+            // then dQ += dS(t) K_t, which overlaps that pass.  S(t+1) goes to the
+            // other S buffer, whose dS(t-1) was read by dQ(t-1), issued earlier.
+            bool ok = mbar_wait(qd_full, 0, abort_flag) && mbar_wait(&kv_full[0], 0, abort_flag);
+            if (ok) {
                 tc_fence_after();
-                issue_dq(n_kv - 1);
-                mma_commit(acc_full);
+                issue_sdp(0);
             }
+            for (int t = 0; ok && t < n_kv; ++t) {
+                if (!(ok = mbar_wait(p_full, t & 1, abort_flag))) break;
+                tc_fence_after();
+                if (t + 1 < n_kv) {
+                    if (!(ok = mbar_wait(&kv_full[(t + 1) % NS], ((t + 1) / NS) & 1, abort_flag))) break;
+                    tc_fence_after();
+                    issue_sdp(t + 1);
+                }
+                issue_dq(t);
+            }
+            if (ok) mma_commit(acc_full);
             mma_commit(mma_done);
             volatile int never = 0;
             mbar_wait(mma_done, 0, &never);
         }
     } else {
-        // ------------------------------------------------------------ elementwise warps 0-3
-        const int r = warp * 32 + lane;  // tile row == tensor-memory lane
+        // ------------------------------------------------------------ elementwise warps
+        const int quarter = warp & 3, half = warp >> 2;
+        const int r = quarter * 32 + lane;  // tile row == tensor-memory lane
         const int row = qt * 128 + r;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         float b = 0.f, delta = 0.f;
         if (row < p.S) {
             const float2 st = p.rowstat[static_cast<size_t>(bh) * p.S_pad + row];
@@ -290,10 +313,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             int lim = p.S - t * 128;  // keys [lim, 128) of this tile are masked for this row
             if (p.causal) lim = min(lim, row - t * 128 + 1);
             const bool masked = __any_sync(0xffffffffu, lim < 128);
+            const uint32_t sbuf = lane_base + col_sbuf<D>(t & 1);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * half + cc;  // 32-key chunk
                 uint32_t sv[32], dv[32];
-                tmem_ld32(lane_base + kColS + c * 32, sv);
+                tmem_ld32(sbuf + c * 32, sv);
                 tmem_ld32(lane_base + kColDP + c * 32, dv);
                 tmem_wait_ld();
                 uint32_t w[16];
@@ -309,8 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mul2(e, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), nd2));
                     w[i] = pack2<BF16>(g.x, g.y);
                 }
-                // Columns [16c, 16c + 16) of S were read in this or an earlier chunk.
-                tmem_st16(lane_base + kColS + c * 16, w);
+                // Columns [64 half + 16 cc, + 16) of S were read in this or the previous chunk.
+                tmem_st16(sbuf + half * 64 + cc * 16, w);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -322,7 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             // Every MMA has completed: Q's shared memory stages the dQ tile.
 #pragma unroll
-            for (int cc = 0; cc < D / 32; ++cc) {
+            for (int i = 0; i < D / 64; ++i) {
+                const int cc = half * (D / 64) + i;  // 32-column chunk of dQ
                 uint32_t o[32];
                 tmem_ld32(lane_base + kColAcc + cc * 32, o);
                 tmem_wait_ld();
@@ -412,10 +438,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&qd_empty[s], 1);
         }
         mbar_init(sd_full, 1);
-        mbar_init(p_full, 4);
+        mbar_init(p_full, kElemWarps);
         mbar_init(acc_full, 1);
         mbar_init(mma_done, 1);
-        mbar_init(staged, 4);
+        mbar_init(staged, kElemWarps);
         *abort_flag = (*reinterpret_cast<volatile unsigned int *>(&g_device_error) != 0u) ? 1 : 0;
         fence_mbarrier_init();
     }
@@ -477,11 +503,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t do_addr = q_addr + TILE;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(tmem + kColAcc, tmem + kColS + kk * 8, smem_desc_sw128(do_addr + kk * 2048, kBoxBytes, 1024),
+                    mma_ts(tmem + kColAcc, tmem + kColS + packed_col(kk), smem_desc_sw128(do_addr + kk * 2048, kBoxBytes, 1024),
                            kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(tmem + kColAcc + D, tmem + kColDP + kk * 8,
+                    mma_ts(tmem + kColAcc + D, tmem + kColDP + packed_col(kk),
                            smem_desc_sw128(q_addr + kk * 2048, kBoxBytes, 1024), kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
                 mma_commit(&qd_empty[s]);
             };
@@ -521,10 +547,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait(mma_done, 0, &never);
         }
     } else {
-        // ------------------------------------------------------------ elementwise warps 0-3
-        const int r = warp * 32 + lane;  // key row of the tile == tensor-memory lane
+        // ------------------------------------------------------------ elementwise warps
+        const int quarter = warp & 3, half = warp >> 2;
+        const int r = quarter * 32 + lane;  // key row of the tile == tensor-memory lane
         const int key = kt * 128 + r;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const float c2 = p.scale_log2;
         bool ok = true;
         for (int x = 0; x < n_q; ++x) {
@@ -536,7 +563,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int hi = p.S - qbase;                  // queries [hi, 128) are past the end
             const bool masked = __any_sync(0xffffffffu, lo > 0 || hi < 128);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * half + cc;  // 32-query chunk
                 uint32_t sv[32], dv[32];
                 tmem_ld32(lane_base + kColS + c * 32, sv);
                 tmem_ld32(lane_base + kColDP + c * 32, dv);
@@ -557,8 +585,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     wp[i] = pack2<BF16>(pp.x, pp.y);
                     wd[i] = pack2<BF16>(g.x, g.y);
                 }
-                tmem_st16(lane_base + kColS + c * 16, wp);
-                tmem_st16(lane_base + kColDP + c * 16, wd);
+                tmem_st16(lane_base + kColS + half * 64 + cc * 16, wp);
+                tmem_st16(lane_base + kColDP + half * 64 + cc * 16, wd);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -570,7 +598,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             // Every MMA has completed: K's and V's shared memory stage dV and dK.
 #pragma unroll
-            for (int cc = 0; cc < D / 32; ++cc) {
+            for (int i = 0; i < D / 64; ++i) {
+                const int cc = half * (D / 64) + i;  // 32-column chunk of dV and dK
                 uint32_t o[32];
                 tmem_ld32(lane_base + kColAcc + cc * 32, o);
                 tmem_wait_ld();
