@@ -133,12 +133,16 @@ struct CfgQ {
     static_assert(D == 64 || D == 128, "head size 64 or 128");
     static constexpr int kBoxes = D / kBoxCols;
     static constexpr int kTile = kBoxes * kBoxBytes;
-    static constexpr int kStages = (D == 64) ? 4 : 2;  // (K, V) tile pairs in flight
+    // K(t) is read by S(t), issued one key tile ahead, and by dQ(t): three K
+    // tiles are live at once; V(t) only by dP(t).
+    static constexpr int kKStages = (D == 64) ? 4 : 3;
+    static constexpr int kVStages = (D == 64) ? 4 : 2;
     static constexpr int kOffQ = 0;
     static constexpr int kOffDO = kTile;
-    static constexpr int kOffRing = 2 * kTile;  // stage s: K at +2 s kTile, V at +(2 s + 1) kTile
-    static constexpr int kOffBars = kOffRing + 2 * kStages * kTile;
-    static constexpr int kNumBars = 1 + 2 * kStages + 5;
+    static constexpr int kOffK = 2 * kTile;
+    static constexpr int kOffV = kOffK + kKStages * kTile;
+    static constexpr int kOffBars = kOffV + kVStages * kTile;
+    static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 7;
     static constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
     static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -150,20 +154,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tm_dq, const Params p) {
     using namespace ptx;
     using C = CfgQ<D>;
-    constexpr int NS = C::kStages;
+    constexpr int KS = C::kKStages;
+    constexpr int VS = C::kVStages;
     constexpr int TILE = C::kTile;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t *sQ = smem + C::kOffQ;
     uint8_t *sDO = smem + C::kOffDO;
-    uint8_t *sRing = smem + C::kOffRing;
+    uint8_t *sK = smem + C::kOffK;  // [KS][TILE]
+    uint8_t *sV = smem + C::kOffV;  // [VS][TILE]
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kOffBars);
     uint64_t *qd_full = bars;
-    uint64_t *kv_full = bars + 1;      // [NS]
-    uint64_t *kv_empty = kv_full + NS;  // [NS]
-    uint64_t *sd_full = kv_empty + NS;
-    uint64_t *p_full = sd_full + 1;
+    uint64_t *k_full = bars + 1;       // [KS]
+    uint64_t *k_empty = k_full + KS;   // [KS]
+    uint64_t *v_full = k_empty + KS;   // [VS]
+    uint64_t *v_empty = v_full + VS;   // [VS]
+    uint64_t *s_full = v_empty + VS;   // [2]: S(t) in S buffer t % 2
+    uint64_t *dp_full = s_full + 2;    // dP(t) in the dP buffer
+    uint64_t *p_full = dp_full + 1;    // dS(t) packed (S(t) and dP(t) read)
     uint64_t *acc_full = p_full + 1;
     uint64_t *mma_done = acc_full + 1;
     uint64_t *staged = mma_done + 1;
@@ -179,11 +188,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(qd_full, 1);
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+        for (int s = 0; s < KS; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
         }
-        mbar_init(sd_full, 1);
+        for (int s = 0; s < VS; ++s) {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(dp_full, 1);
         mbar_init(p_full, kElemWarps);
         mbar_init(acc_full, 1);
         mbar_init(mma_done, 1);
@@ -216,20 +231,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             int issued = 0;
             for (int t = 0; t < n_kv; ++t) {
-                const int s = t % NS;
-                if (t >= NS && !mbar_wait(&kv_empty[s], ((t / NS) - 1) & 1, abort_flag)) break;
-                uint8_t *sk = sRing + 2 * s * TILE;
-                mbar_arrive_expect_tx(&kv_full[s], 2 * TILE);
-                for (int b = 0; b < C::kBoxes; ++b) {
-                    tma_load_3d(sk + b * kBoxBytes, &tm_k, &kv_full[s], b * kBoxCols, t * 128, bh);
-                    tma_load_3d(sk + TILE + b * kBoxBytes, &tm_v, &kv_full[s], b * kBoxCols, t * 128, bh);
+                const int sk = t % KS, sv = t % VS;
+                if (t >= KS && !mbar_wait(&k_empty[sk], ((t / KS) - 1) & 1, abort_flag)) break;
+                mbar_arrive_expect_tx(&k_full[sk], TILE);
+                for (int b = 0; b < C::kBoxes; ++b)
+                    tma_load_3d(sK + sk * TILE + b * kBoxBytes, &tm_k, &k_full[sk], b * kBoxCols, t * 128, bh);
+                if (t >= VS && !mbar_wait(&v_empty[sv], ((t / VS) - 1) & 1, abort_flag)) {
+                    issued = -(t + 1);  // K(t) issued, V(t) not
+                    break;
                 }
+                mbar_arrive_expect_tx(&v_full[sv], TILE);
+                for (int b = 0; b < C::kBoxes; ++b)
+                    tma_load_3d(sV + sv * TILE + b * kBoxBytes, &tm_v, &v_full[sv], b * kBoxCols, t * 128, bh);
                 issued = t + 1;
             }
             if (*abort_flag) {
+                // Let the copies already issued land before shared memory is released.
                 volatile int never = 0;
                 mbar_wait(qd_full, 0, &never);
-                for (int t = max(0, issued - NS); t < issued; ++t) mbar_wait(&kv_full[t % NS], (t / NS) & 1, &never);
+                const int nk = issued < 0 ? -issued : issued;  // K tiles issued
+                const int nv = issued < 0 ? -issued - 1 : issued;
+                for (int i = max(0, nk - KS); i < nk; ++i) mbar_wait(&k_full[i % KS], (i / KS) & 1, &never);
+                for (int i = max(0, nv - VS); i < nv; ++i) mbar_wait(&v_full[i % VS], (i / VS) & 1, &never);
             }
         }
     } else if (warp == kWarpMma) {
@@ -240,50 +263,58 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t do_addr = smem_u32(sDO);
             // dQ += dS(t) K_t: dS from tensor memory, K_t (keys x D, D contiguous) as an MN-major B.
             auto issue_dq = [&](int t) {
-                const int s = t % NS;
-                const uint32_t k_addr = smem_u32(sRing + 2 * s * TILE);
+                const uint32_t k_addr = smem_u32(sK + (t % KS) * TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma_ts(tmem + kColAcc, tmem + col_sbuf<D>(t & 1) + packed_col(kk),
                            smem_desc_sw128(k_addr + kk * 2048, kBoxBytes, 1024), kIdAcc, (t > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(&kv_empty[s]);
+                mma_commit(&k_empty[t % KS]);
             };
-            // S(t) and dP(t) of key tile t into S buffer t % 2 and the dP buffer.
-            auto issue_sdp = [&](int t) {
-                const int s = t % NS;
-                const uint32_t k_addr = smem_u32(sRing + 2 * s * TILE);
-                const uint32_t v_addr = k_addr + TILE;
-                const uint32_t d_s = tmem + col_sbuf<D>(t & 1);
+            auto issue_s = [&](int t) {
+                const uint32_t k_addr = smem_u32(sK + (t % KS) * TILE);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tmem + col_sbuf<D>(t & 1), smem_desc_sw128(q_addr + off, 16, 1024),
+                           smem_desc_sw128(k_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&s_full[t & 1]);
+            };
+            auto issue_dp = [&](int t) {
+                const uint32_t v_addr = smem_u32(sV + (t % VS) * TILE);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
                     mma_ss(tmem + kColDP, smem_desc_sw128(do_addr + off, 16, 1024),
                            smem_desc_sw128(v_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
                 }
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                    mma_ss(d_s, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
-                           kIdS, kk > 0 ? 1u : 0u);
-                }
-                mma_commit(sd_full);
+                mma_commit(dp_full);
+                mma_commit(&v_empty[t % VS]);
             };
-            // Per key tile t, once the elementwise warps are done with S(t), dP(t):
-            // dP(t+1) and S(t+1) first (the next elementwise pass waits on them),
-            // then dQ += dS(t) K_t, which overlaps that pass.  S(t+1) goes to the
-            // other S buffer, whose dS(t-1) was read by dQ(t-1), issued earlier.
-            bool ok = mbar_wait(qd_full, 0, abort_flag) && mbar_wait(&kv_full[0], 0, abort_flag);
+            auto wait_k = [&](int t) { return mbar_wait(&k_full[t % KS], (t / KS) & 1, abort_flag); };
+            auto wait_v = [&](int t) { return mbar_wait(&v_full[t % VS], (t / VS) & 1, abort_flag); };
+            // Key tile t: S(t+1) goes out as soon as dQ(t-1) (the last reader of
+            // its buffer) has been issued, so the elementwise warps' exps of
+            // tile t+1 start right after they finish tile t; dP(t+1) waits for
+            // them to have read dP(t); dQ(t) last.
+            bool ok = mbar_wait(qd_full, 0, abort_flag) && wait_k(0) && wait_v(0);
             if (ok) {
                 tc_fence_after();
-                issue_sdp(0);
+                issue_s(0);
+                issue_dp(0);
             }
             for (int t = 0; ok && t < n_kv; ++t) {
+                if (t + 1 < n_kv) {
+                    if (!(ok = wait_k(t + 1))) break;
+                    tc_fence_after();
+                    issue_s(t + 1);
+                }
                 if (!(ok = mbar_wait(p_full, t & 1, abort_flag))) break;
                 tc_fence_after();
                 if (t + 1 < n_kv) {
-                    if (!(ok = mbar_wait(&kv_full[(t + 1) % NS], ((t + 1) / NS) & 1, abort_flag))) break;
+                    if (!(ok = wait_v(t + 1))) break;
                     tc_fence_after();
-                    issue_sdp(t + 1);
+                    issue_dp(t + 1);
                 }
                 issue_dq(t);
             }
@@ -308,33 +339,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float2 nd2 = make_float2(-delta, -delta);
         bool ok = true;
         for (int t = 0; t < n_kv; ++t) {
-            if (!(ok = mbar_wait_warp(sd_full, t & 1, abort_flag))) break;
-            tc_fence_after();
             int lim = p.S - t * 128;  // keys [lim, 128) of this tile are masked for this row
             if (p.causal) lim = min(lim, row - t * 128 + 1);
             const bool masked = __any_sync(0xffffffffu, lim < 128);
             const uint32_t sbuf = lane_base + col_sbuf<D>(t & 1);
+            // Phase 1: e = 2^(S c2 - b) for this warp's 64 keys.
+            if (!(ok = mbar_wait_warp(&s_full[t & 1], (t >> 1) & 1, abort_flag))) break;
+            tc_fence_after();
+            float ev[64];
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * half + cc;  // 32-key chunk
-                uint32_t sv[32], dv[32];
+                uint32_t sv[32];
                 tmem_ld32(sbuf + c * 32, sv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float s0 = __uint_as_float(sv[i]);
+                    if (masked && c * 32 + i >= lim) s0 = -INFINITY;
+                    ev[cc * 32 + i] = ex2_approx(fmaf(s0, c2, -b));
+                }
+            }
+            // Phase 2: dS = e (dP - delta), packed into the S buffer's columns
+            // this warp has read.
+            if (!(ok = mbar_wait_warp(dp_full, t & 1, abort_flag))) break;
+            tc_fence_after();
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * half + cc;
+                uint32_t dv[32];
                 tmem_ld32(lane_base + kColDP + c * 32, dv);
                 tmem_wait_ld();
                 uint32_t w[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    float s0 = __uint_as_float(sv[2 * i]), s1 = __uint_as_float(sv[2 * i + 1]);
-                    if (masked) {
-                        if (c * 32 + 2 * i >= lim) s0 = -INFINITY;
-                        if (c * 32 + 2 * i + 1 >= lim) s1 = -INFINITY;
-                    }
-                    const float2 e = make_float2(ex2_approx(fmaf(s0, c2, -b)), ex2_approx(fmaf(s1, c2, -b)));
-                    const float2 g =
-                        mul2(e, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), nd2));
+                    const float2 g = mul2(make_float2(ev[cc * 32 + 2 * i], ev[cc * 32 + 2 * i + 1]),
+                                          add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])),
+                                               nd2));
                     w[i] = pack2<BF16>(g.x, g.y);
                 }
-                // Columns [64 half + 16 cc, + 16) of S were read in this or the previous chunk.
                 tmem_st16(sbuf + half * 64 + cc * 16, w);
             }
             tmem_wait_st();
@@ -388,7 +431,7 @@ struct CfgKV {
     static constexpr int kOffV = kTile;
     static constexpr int kOffRing = 2 * kTile;
     static constexpr int kOffBars = kOffRing + kStages * kStage;
-    static constexpr int kNumBars = 1 + 2 * kStages + 5;
+    static constexpr int kNumBars = 1 + 2 * kStages + 7;
     static constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
     static_assert(kStage % 1024 == 0, "stage alignment");
     static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -415,9 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *kv_full = bars;
     uint64_t *qd_full = bars + 1;       // [NS]
     uint64_t *qd_empty = qd_full + NS;  // [NS]
-    uint64_t *sd_full = qd_empty + NS;
-    uint64_t *p_full = sd_full + 1;
-    uint64_t *acc_full = p_full + 1;
+    uint64_t *s_full = qd_empty + NS;   // S^T(x) in tensor memory
+    uint64_t *dp_full = s_full + 1;     // dP^T(x) in tensor memory
+    uint64_t *p1_full = dp_full + 1;    // P^T(x) packed (S^T read)
+    uint64_t *p2_full = p1_full + 1;    // dS^T(x) packed (dP^T read)
+    uint64_t *acc_full = p2_full + 1;
     uint64_t *mma_done = acc_full + 1;
     uint64_t *staged = mma_done + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(staged + 1);
@@ -437,8 +482,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&qd_full[s], 1);
             mbar_init(&qd_empty[s], 1);
         }
-        mbar_init(sd_full, 1);
-        mbar_init(p_full, kElemWarps);
+        mbar_init(s_full, 1);
+        mbar_init(dp_full, 1);
+        mbar_init(p1_full, kElemWarps);
+        mbar_init(p2_full, kElemWarps);
         mbar_init(acc_full, 1);
         mbar_init(mma_done, 1);
         mbar_init(staged, kElemWarps);
@@ -495,53 +542,70 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t kIdAcc = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
             const uint32_t k_addr = smem_u32(sK);
             const uint32_t v_addr = smem_u32(sV);
-            // dV += P^T(x) dO_x and dK += dS^T(x) Q_x: A from tensor memory, the
-            // query-tile operands (queries x D, D contiguous) as MN-major B.
-            auto issue_grads = [&](int x) {
-                const int s = x % NS;
-                const uint32_t q_addr = smem_u32(sRing + s * STAGE);
-                const uint32_t do_addr = q_addr + TILE;
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(tmem + kColAcc, tmem + kColS + packed_col(kk), smem_desc_sw128(do_addr + kk * 2048, kBoxBytes, 1024),
-                           kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(tmem + kColAcc + D, tmem + kColDP + packed_col(kk),
-                           smem_desc_sw128(q_addr + kk * 2048, kBoxBytes, 1024), kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(&qd_empty[s]);
-            };
-            bool ok = mbar_wait(kv_full, 0, abort_flag);
-            for (int x = 0; ok && x < n_q; ++x) {
-                const int s = x % NS;
-                if (!(ok = mbar_wait(&qd_full[s], (x / NS) & 1, abort_flag))) break;
-                if (x > 0) {
-                    if (!(ok = mbar_wait(p_full, (x - 1) & 1, abort_flag))) break;
-                    tc_fence_after();
-                    issue_grads(x - 1);
-                }
-                tc_fence_after();
-                const uint32_t q_addr = smem_u32(sRing + s * STAGE);
-                const uint32_t do_addr = q_addr + TILE;
+            // Two chains per query tile x, each hidden behind the other's
+            // elementwise phase:
+            //   phase 1 (S^T -> P^T) -> dV(x) += P^T dO_x -> S^T(x+1)  (S buffer)
+            //   phase 2 (dP^T -> dS^T) -> dK(x) += dS^T Q_x -> dP^T(x+1)  (dP buffer)
+            // Each buffer is overwritten only after the product that reads its
+            // packed 16-bit half (one thread's MMAs execute in order).
+            auto stage_addr = [&](int x) { return smem_u32(sRing + (x % NS) * STAGE); };
+            auto issue_s = [&](int x) {
+                const uint32_t q_addr = stage_addr(x);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
                     mma_ss(tmem + kColS, smem_desc_sw128(k_addr + off, 16, 1024),
                            smem_desc_sw128(q_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
                 }
+                mma_commit(s_full);
+            };
+            auto issue_dp = [&](int x) {
+                const uint32_t do_addr = stage_addr(x) + TILE;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
                     mma_ss(tmem + kColDP, smem_desc_sw128(v_addr + off, 16, 1024),
                            smem_desc_sw128(do_addr + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(sd_full);
-            }
-            if (ok && n_q > 0 && (ok = mbar_wait(p_full, (n_q - 1) & 1, abort_flag))) {
+                mma_commit(dp_full);
+            };
+            // The query-tile operands (queries x D, D contiguous) as MN-major B.
+            auto issue_dv = [&](int x) {
+                const uint32_t do_addr = stage_addr(x) + TILE;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(tmem + kColAcc, tmem + kColS + packed_col(kk),
+                           smem_desc_sw128(do_addr + kk * 2048, kBoxBytes, 1024), kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
+            };
+            auto issue_dk = [&](int x) {
+                const uint32_t q_addr = stage_addr(x);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(tmem + kColAcc + D, tmem + kColDP + packed_col(kk),
+                           smem_desc_sw128(q_addr + kk * 2048, kBoxBytes, 1024), kIdAcc, (x > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&qd_empty[x % NS]);  // the last product reading stage x % NS
+            };
+            bool ok = mbar_wait(kv_full, 0, abort_flag) && mbar_wait(&qd_full[0], 0, abort_flag);
+            if (ok) {
                 tc_fence_after();
-                issue_grads(n_q - 1);
-                mma_commit(acc_full);
+                issue_s(0);
+                issue_dp(0);
             }
+            for (int x = 0; ok && x < n_q; ++x) {
+                if (!(ok = mbar_wait(p1_full, x & 1, abort_flag))) break;
+                tc_fence_after();
+                issue_dv(x);
+                if (x + 1 < n_q) {
+                    if (!(ok = mbar_wait(&qd_full[(x + 1) % NS], ((x + 1) / NS) & 1, abort_flag))) break;
+                    tc_fence_after();
+                    issue_s(x + 1);
+                }
+                if (!(ok = mbar_wait(p2_full, x & 1, abort_flag))) break;
+                tc_fence_after();
+                issue_dk(x);
+                if (x + 1 < n_q) issue_dp(x + 1);
+            }
+            if (ok) mma_commit(acc_full);
             mma_commit(mma_done);
             volatile int never = 0;
             mbar_wait(mma_done, 0, &never);
@@ -555,21 +619,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float c2 = p.scale_log2;
         bool ok = true;
         for (int x = 0; x < n_q; ++x) {
-            if (!(ok = mbar_wait_warp(sd_full, x & 1, abort_flag))) break;
-            tc_fence_after();
             const float4 *st = reinterpret_cast<const float4 *>(sRing + (x % NS) * STAGE + 2 * TILE);
             const int qbase = (i0 + x) * 128;
             const int lo = p.causal ? key - qbase : 0;  // queries [0, lo) precede this key
             const int hi = p.S - qbase;                  // queries [hi, 128) are past the end
             const bool masked = __any_sync(0xffffffffu, lo > 0 || hi < 128);
+            // Phase 1: P^T = 2^(S^T c2 - b) for this warp's 64 queries, kept in
+            // fp32 for phase 2 and packed to 16 bits for dV.
+            if (!(ok = mbar_wait_warp(s_full, x & 1, abort_flag))) break;
+            tc_fence_after();
+            float pv[64];
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * half + cc;  // 32-query chunk
-                uint32_t sv[32], dv[32];
+                uint32_t sv[32];
                 tmem_ld32(lane_base + kColS + c * 32, sv);
-                tmem_ld32(lane_base + kColDP + c * 32, dv);
                 tmem_wait_ld();
-                uint32_t wp[16], wd[16];
+                uint32_t wp[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int n0 = c * 32 + 2 * i;
@@ -579,19 +645,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (n0 < lo || n0 >= hi) s0 = -INFINITY;
                         if (n0 + 1 < lo || n0 + 1 >= hi) s1 = -INFINITY;
                     }
-                    const float2 pp = make_float2(ex2_approx(fmaf(s0, c2, -bd.x)), ex2_approx(fmaf(s1, c2, -bd.z)));
-                    const float2 g = mul2(pp, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])),
-                                                   make_float2(-bd.y, -bd.w)));
-                    wp[i] = pack2<BF16>(pp.x, pp.y);
-                    wd[i] = pack2<BF16>(g.x, g.y);
+                    pv[cc * 32 + 2 * i] = ex2_approx(fmaf(s0, c2, -bd.x));
+                    pv[cc * 32 + 2 * i + 1] = ex2_approx(fmaf(s1, c2, -bd.z));
+                    wp[i] = pack2<BF16>(pv[cc * 32 + 2 * i], pv[cc * 32 + 2 * i + 1]);
                 }
                 tmem_st16(lane_base + kColS + half * 64 + cc * 16, wp);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p1_full);
+            // Phase 2: dS^T = P^T (dP^T - delta), packed to 16 bits for dK.
+            if (!(ok = mbar_wait_warp(dp_full, x & 1, abort_flag))) break;
+            tc_fence_after();
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * half + cc;
+                uint32_t dv[32];
+                tmem_ld32(lane_base + kColDP + c * 32, dv);
+                tmem_wait_ld();
+                uint32_t wd[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int n0 = c * 32 + 2 * i;
+                    const float4 bd = st[n0 >> 1];
+                    const float2 g =
+                        mul2(make_float2(pv[cc * 32 + 2 * i], pv[cc * 32 + 2 * i + 1]),
+                             add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])),
+                                  make_float2(-bd.y, -bd.w)));
+                    wd[i] = pack2<BF16>(g.x, g.y);
+                }
                 tmem_st16(lane_base + kColDP + half * 64 + cc * 16, wd);
             }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(p2_full);
         }
         if (ok) ok = mbar_wait_warp(acc_full, 0, abort_flag);
         if (ok) {
