@@ -160,8 +160,11 @@ int pmkl_causal_attention_bwd(const void *dout, const void *q, const void *k, co
                               size_t workspace_bytes, void *stream);
 
 /* As pmkl_causal_attention_bwd with an explicit kernel choice: PMKL_ATTN_AUTO,
- * PMKL_ATTN_SIMT or PMKL_ATTN_TCGEN05 (PMKL_ERR_UNSUPPORTED when the tensor-core
- * path does not cover the arguments). */
+ * PMKL_ATTN_SIMT, PMKL_ATTN_TCGEN05 (PMKL_ERR_UNSUPPORTED when the tensor-core
+ * path does not cover the arguments), or PMKL_ATTN_TCGEN05_SIMPLE: the
+ * tensor-core gradient kernels with the per-row term delta taken the long way
+ * (a forward writing fp32 O, m, l, then a row-statistics kernel) instead of
+ * from the persistent forward's epilogue (comparison only). */
 int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k, const void *v, const void *m,
                                  const void *l, void *dq, void *dk, void *dv, int batch, int heads, int seq,
                                  int hidden, int dtype, int is_causal, float scale, void *workspace,

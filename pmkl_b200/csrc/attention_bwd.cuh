@@ -9,12 +9,14 @@
 //   dS_nj = p_nj (dP_nj - delta_n)
 //   dQ = scale dS K,   dK = scale dS^T Q,   dV = P^T dO
 // (the reference's innermost loop, :99-121, sums exactly scale p_nm (dP_nm -
-// delta_n) for each (n, m)).  Three launches, no atomics, deterministic:
-//   1. bwd_rowstat_kernel: per query row, b_n = m~_n log2 e + log2 l~_n (so
-//      that p = 2^(s c2 - b_n) with c2 = scale log2 e) and delta_n.  delta
-//      comes from this library's own forward (O, m, l in fp32) through
+// delta_n) for each (n, m)).  Three steps, no atomics, deterministic:
+//   1. per query row, b_n = m~_n log2 e + log2 l~_n (so that p = 2^(s c2 - b_n)
+//      with c2 = scale log2 e) and delta_n, from this library's own forward:
 //        sum_j p_nj dP_nj = exp(m_n - m~_n) (l_n / l~_n) (dO_n . O_n),
-//      exact algebra, because the reference backward takes no O.
+//      exact algebra, because the reference backward takes no O.  The
+//      persistent forward forms them in its epilogue (attention_pp.cuh,
+//      DeltaParams); otherwise a forward writes fp32 O, m, l and
+//      bwd_rowstat_kernel forms them.
 //   2. attn_bwd_dq_kernel: one CTA per (slice, 128-row query tile); per key
 //      tile S = Q K^T and dP = dO V^T into tensor memory, dS (16-bit) back
 //      into tensor memory, dQ += dS K.

@@ -88,6 +88,18 @@ struct Params {
     void *l_out;
 };
 
+// The backward's instantiation writes row statistics instead of O, m, l: for
+// each query row, b = m~ log2 e + log2 l~ and delta = exp(m - m~) (l / l~)
+// (dO . O), with m~, l~ the caller's statistics (input dtype) and m, l, O this
+// kernel's own; rows in [S, S_pad) get (0, 0).
+struct DeltaParams {
+    int S_pad;
+    const void *dout;      // [BH][S][D], input dtype, contiguous
+    const void *m_given;   // [BH][S]
+    const void *l_given;
+    float2 *rowstat;       // [BH][S_pad]
+};
+
 struct Unit {
     int bh;
     int row0;     // first row of tile A
@@ -187,11 +199,13 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2,
 #define PMKL_PP_NPOLY 0
 #endif
 
-template <int D, bool BF16, int NPOLY = PMKL_PP_NPOLY>
+// DELTA: the backward's instantiation, writing the row statistics (b, delta)
+// instead of O, m, l (DeltaParams).
+template <int D, bool BF16, int NPOLY = PMKL_PP_NPOLY, bool DELTA = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                       const Params p) {
+                       const Params p, const DeltaParams dpar) {
     using namespace ptx;
     using C = Cfg<D>;
     constexpr int NS = C::kStages;
@@ -530,6 +544,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t oa = lane_base + col_o(x);
                     const int bb = w.bh / p.H;
                     const int hh = w.bh - bb * p.H;
+                    if constexpr (DELTA) {
+                        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+                        const size_t ridx = static_cast<size_t>(w.bh) * p.S + row;
+                        const uint4 *drow = reinterpret_cast<const uint4 *>(static_cast<const T *>(dpar.dout) + ridx * D);
+                        float dot = 0.f;
+#pragma unroll
+                        for (int cc = 0; cc < D / 32; ++cc) {
+                            uint32_t o[32];
+                            tmem_ld32(oa + cc * 32, o);
+                            tmem_wait_ld();
+                            if (cc == D / 32 - 1) {
+                                tc_fence_before();
+                                __syncwarp();
+                                if (lane == 0) mbar_arrive(&o_empty[x]);
+                            }
+                            if (row < p.S) {
+#pragma unroll
+                                for (int q4 = 0; q4 < 4; ++q4) {
+                                    const uint4 dv = __ldg(drow + cc * 4 + q4);
+                                    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e) {
+                                        float d0, d1;
+                                        tc::unpack2<BF16>(dw[e], d0, d1);
+                                        dot = fmaf(__uint_as_float(o[q4 * 8 + 2 * e]), d0, dot);
+                                        dot = fmaf(__uint_as_float(o[q4 * 8 + 2 * e + 1]), d1, dot);
+                                    }
+                                }
+                            }
+                        }
+                        float2 rs = make_float2(0.f, 0.f);
+                        if (row < p.S) {
+                            const float mg = Elem<T>::to_float(static_cast<const T *>(dpar.m_given)[ridx]);
+                            const float lg = Elem<T>::to_float(static_cast<const T *>(dpar.l_given)[ridx]);
+                            const float l_true = (m_true == -INFINITY) ? 0.f : l * ex2_approx((m_used - m_true) * c2);
+                            const float f = expf(m_true * p.scale - mg) * (l_true / lg);
+                            rs = make_float2(mg * 1.4426950408889634f + log2f(lg), f * dot * inv_l);
+                        }
+                        dpar.rowstat[static_cast<size_t>(w.bh) * dpar.S_pad + row] = rs;
+                        continue;
+                    }
                     if (p.out_dtype == PMKL_DTYPE_F32) {
                         float *orow = static_cast<float *>(p.o_f32) + bb * p.o_sb + hh * p.o_sh + row * p.o_ss;
 #pragma unroll

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "pmkl_b200.h"
 
 namespace pmkl_b200 {

@@ -200,12 +200,12 @@ int sm_count() {
 // The persistent kernel re-splits its registers between warpgroups with
 // setmaxnreg; the split only fits when the kernel was built with exactly
 // pp::kLaunchRegs registers per thread.  Checked once per process.
-template <int D, bool BF16>
+template <int D, bool BF16, bool DELTA = false>
 bool pp_launchable() {
     static int ok = -1;
     if (ok < 0) {
         cudaFuncAttributes attr;
-        ok = (cudaFuncGetAttributes(&attr, pp::attn_fwd_pp_kernel<D, BF16>) == cudaSuccess &&
+        ok = (cudaFuncGetAttributes(&attr, pp::attn_fwd_pp_kernel<D, BF16, PMKL_PP_NPOLY, DELTA>) == cudaSuccess &&
               attr.numRegs == pp::kLaunchRegs)
                  ? 1
                  : 0;
@@ -214,13 +214,25 @@ bool pp_launchable() {
     return ok == 1;
 }
 
+// Backward's use of the persistent forward: instead of O, m, l it writes the
+// row statistics (b, delta) from dO and the caller's m~, l~.
+struct DeltaArgs {
+    const void *dout;
+    const void *m_given;
+    const void *l_given;
+    float2 *rowstat;
+    int S_pad;
+};
+
 template <int D, bool BF16>
 int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int BH, int causal,
-              float scale, int dtype, int out_dtype, const AttnLayout &lay, cudaStream_t stream) {
+              float scale, int dtype, int out_dtype, const AttnLayout &lay, cudaStream_t stream,
+              const DeltaArgs *delta = nullptr) {
     using C = pp::Cfg<D>;
     static std::once_flag smem_once[kMaxDevices];
-    auto kernel = pp::attn_fwd_pp_kernel<D, BF16>;
-    if (!ensure_smem(kernel, C::kSmemBytes, smem_once)) return PMKL_ERR_LAUNCH;
+    static std::once_flag smem_once_delta[kMaxDevices];
+    auto kernel = delta ? pp::attn_fwd_pp_kernel<D, BF16, PMKL_PP_NPOLY, true> : pp::attn_fwd_pp_kernel<D, BF16>;
+    if (!ensure_smem(kernel, C::kSmemBytes, delta ? smem_once_delta : smem_once)) return PMKL_ERR_LAUNCH;
     CUtensorMap tq, tk, tv, to;
     const bool o16 = out_dtype != PMKL_DTYPE_F32;
     const int B = BH / lay.H, Hkv = lay.H / lay.kv_group;
@@ -256,8 +268,10 @@ int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, voi
     p.o_f32 = o;
     p.m_out = m;
     p.l_out = l;
+    pp::DeltaParams dp{};
+    if (delta) dp = pp::DeltaParams{delta->S_pad, delta->dout, delta->m_given, delta->l_given, delta->rowstat};
     const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
-    kernel<<<grid, pp::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+    kernel<<<grid, pp::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, p, dp);
     return launch_status();
 }
 
@@ -314,7 +328,7 @@ int select_kernel(const void *q, const void *k, const void *v, const void *o, in
     const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype, lay);
     // The one-tile kernel reads contiguous [B*H, S, D] tensors only.
     const bool simple_ok = tc_ok && layout_contiguous(lay, S, hidden);
-    if (kernel == PMKL_ATTN_TCGEN05 && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
     if (kernel == PMKL_ATTN_TCGEN05_SIMPLE && !simple_ok) return PMKL_ERR_UNSUPPORTED;
     if (kernel == PMKL_ATTN_SIMT || !tc_ok) return PMKL_ATTN_SIMT;
     if (kernel == PMKL_ATTN_TCGEN05_SIMPLE) return PMKL_ATTN_TCGEN05_SIMPLE;
@@ -532,7 +546,8 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
                        void *stream_) {
     if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
     if (!dtype_valid(dtype)) return PMKL_ERR_INVALID_DTYPE;
-    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05)
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
         return PMKL_ERR_UNSUPPORTED;
     const long long BH = static_cast<long long>(batch) * heads;
     if (BH == 0 || seq == 0 || hidden == 0) return PMKL_OK;
@@ -548,7 +563,7 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
     const int bh = static_cast<int>(BH);
     const void *const ptrs[9] = {dout, q, k, v, m, l, dq, dk, dv};
     const bool tc_ok = bwd_tc_applies(ptrs, hidden, dtype);
-    if (kernel == PMKL_ATTN_TCGEN05 && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
     if (tc_ok && kernel != PMKL_ATTN_SIMT) {
         const BwdLayout L = bwd_layout_tc(BH, seq, hidden);
         if (workspace_bytes < L.total) return PMKL_ERR_WORKSPACE;
@@ -557,13 +572,36 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
         float *m32 = reinterpret_cast<float *>(ws + L.m);
         float *l32 = reinterpret_cast<float *>(ws + L.l);
         float2 *rowstat = reinterpret_cast<float2 *>(ws + L.rowstat);
-        // The forward, with fp32 outputs, gives delta = sum_j p dP through dO . O.
-        int rc = attention_impl(q, k, v, o32, m32, l32, batch, heads, seq, hidden, dtype, PMKL_DTYPE_F32, causal, sc,
-                                PMKL_ATTN_AUTO, stream_);
-        if (rc != PMKL_OK) return rc;
-        rc = dtype == PMKL_DTYPE_BF16
-                 ? launch_bwd_rowstat<__nv_bfloat16>(dout, o32, m32, l32, m, l, rowstat, seq, L.S_pad, hidden, BH, stream)
-                 : launch_bwd_rowstat<__half>(dout, o32, m32, l32, m, l, rowstat, seq, L.S_pad, hidden, BH, stream);
+        // delta = sum_j p dP comes from this library's forward through dO . O:
+        // the persistent kernel forms it in its epilogue (O never leaves tensor
+        // memory); otherwise a forward with fp32 O, m, l and the row-statistics
+        // kernel.
+        int rc;
+        const bool bf = dtype == PMKL_DTYPE_BF16;
+        const bool fused = kernel != PMKL_ATTN_TCGEN05_SIMPLE &&
+                           (hidden == 64 ? (bf ? pp_launchable<64, true, true>() : pp_launchable<64, false, true>())
+                                         : (bf ? pp_launchable<128, true, true>() : pp_launchable<128, false, true>()));
+        if (fused) {
+            const DeltaArgs da{dout, m, l, rowstat, L.S_pad};
+            const AttnLayout lay = contiguous_layout(heads, seq, hidden);
+            rc = hidden == 64
+                     ? (bf ? launch_pp<64, true>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal, sc,
+                                                 dtype, dtype, lay, stream, &da)
+                           : launch_pp<64, false>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal, sc,
+                                                  dtype, dtype, lay, stream, &da))
+                     : (bf ? launch_pp<128, true>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal, sc,
+                                                  dtype, dtype, lay, stream, &da)
+                           : launch_pp<128, false>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal,
+                                                   sc, dtype, dtype, lay, stream, &da));
+        } else {
+            rc = attention_impl(q, k, v, o32, m32, l32, batch, heads, seq, hidden, dtype, PMKL_DTYPE_F32, causal, sc,
+                                kernel == PMKL_ATTN_TCGEN05_SIMPLE ? PMKL_ATTN_TCGEN05_SIMPLE : PMKL_ATTN_AUTO,
+                                stream_);
+            if (rc != PMKL_OK) return rc;
+            rc = bf ? launch_bwd_rowstat<__nv_bfloat16>(dout, o32, m32, l32, m, l, rowstat, seq, L.S_pad, hidden, BH,
+                                                        stream)
+                    : launch_bwd_rowstat<__half>(dout, o32, m32, l32, m, l, rowstat, seq, L.S_pad, hidden, BH, stream);
+        }
         if (rc != PMKL_OK) return rc;
         if (dtype == PMKL_DTYPE_BF16)
             return hidden == 64 ? launch_bwd_tc<64, true>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype,

@@ -160,6 +160,21 @@ def test_stats_used_as_given():
     check(do, q, k, v, m2, l2, True, torch.bfloat16, "shifted stats")
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("S", [77, 640])
+def test_delta_routes_agree(S, D):
+    """delta from the persistent forward's epilogue (default) and from an fp32
+    forward plus the row-statistics kernel (PMKL_ATTN_TCGEN05_SIMPLE) feed the
+    same gradient kernels; both match the oracle and each other closely."""
+    t = seeded_bwd_inputs(1, 2, S, D, torch.bfloat16, seed=40 + S + D, causal=True)
+    a = run_bwd(*t, True, kernel=TC)
+    b = run_bwd(*t, True, kernel=3)
+    check(*t, True, torch.bfloat16, f"simple-delta S{S} D{D}", kernel=3)
+    for x, y in zip(a, b):
+        scale = y.float().abs().max().item()
+        assert (x.float() - y.float()).abs().max().item() <= 1e-2 * scale
+
+
 def test_tc_and_simt_agree():
     t = seeded_bwd_inputs(1, 2, 333, 128, torch.bfloat16, seed=24, causal=True)
     a = run_bwd(*t, True, kernel=TC)
@@ -218,7 +233,8 @@ def test_errors():
     assert call(ws.data_ptr(), need - 1) == -9  # PMKL_ERR_WORKSPACE
     assert call(ws.data_ptr() + 16, need) == -4  # workspace not 256-byte aligned
     assert call(0, need) == -3
-    assert call(ws.data_ptr(), need, kernel=3) == -5  # the one-tile forward kernel has no backward
+    assert call(ws.data_ptr(), need, kernel=4) == -5  # no such backward choice
+    assert call(ws.data_ptr(), need, kernel=3, dtype=0) == -5  # fp32 has no tensor-core path
     assert call(ws.data_ptr(), need, kernel=TC, dtype=0) == -5  # fp32 has no tensor-core path
     assert call(ws.data_ptr(), need) == 0
     torch.cuda.synchronize()

@@ -83,7 +83,7 @@ def test_backward_argument_errors():
     assert bwd(L, B=-1) == -1
     assert bwd(L, dtype=7) == -2
     assert bwd(L, kernel=9) == -5
-    assert bwd(L, kernel=3) == -5  # no one-tile backward
+    assert bwd(L, kernel=4) == -5  # no such backward choice
     assert bwd(L, D=300) == -5
     assert bwd(L, ptrs=0) == -3
     assert bwd(L, ws=0) == -3
