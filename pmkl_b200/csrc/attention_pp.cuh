@@ -14,9 +14,9 @@
 //       WG3  warp 12: TMA loads (Q_A, Q_B per unit; K, V through a ring)
 //            warp 13: tcgen05.mma issue (one thread)
 //   * tensor memory: S_A [0,128) S_B [128,256) O_A [256,256+D) O_B [384,384+D).
-//     The softmax writes P (16-bit) into the upper half of its S buffer and,
+//     The softmax writes P (16-bit) into the lower half of its S buffer and,
 //     for tiles whose rows see at most 128 keys, the low part of a hi/lo split
-//     into the lower half; O += P V reads P from tensor memory.
+//     into the upper half; O += P V reads P from tensor memory.
 //   * the MMA thread issues, per key tile j:  PV_A(j), S_A(j+1), PV_B(j),
 //     S_B(j+1).  tcgen05.mma operations of one thread execute in issue order,
 //     so S_X(j+1) (which overwrites P_X(j)) runs after PV_X(j) has read it, and
@@ -25,7 +25,10 @@
 //     the tensor pipe runs PV_B(j) and S_B(j+1), and the other way round.
 //   * the O rescale after a max change is skipped unless the running max grew
 //     by more than 2^8 (the stale max stays the exp2 reference point; the
-//     epilogue corrects m and l once).
+//     epilogue corrects m and l once).  After a row's first key tile the exps
+//     do not wait for the tile's own maximum: they run against the reference
+//     of the earlier tiles while the maximum is gathered alongside, and the
+//     rare tile whose maximum lands far above that reference is redone.
 //   * every wait is bounded (sm100_ptx.cuh); on expiry the CTA drains its own
 //     copies and MMAs, frees tensor memory and reports PMKL_DEVERR_TIMEOUT.
 #pragma once
@@ -44,13 +47,25 @@ constexpr int kWarpMma = 13;
 constexpr uint32_t kTmemCols = 512;
 __host__ __device__ constexpr uint32_t col_s(int x) { return x ? 128u : 0u; }  // S_A, S_B
 __host__ __device__ constexpr uint32_t col_o(int x) { return x ? 384u : 256u; }  // O_A, O_B
-constexpr uint32_t kPHi = 64;  // P (hi) columns inside an S buffer
-constexpr uint32_t kPLo = 0;   // P (lo) columns inside an S buffer
+// P (hi) lives in the lower half of its S buffer: the columns of scores 0-63,
+// which the softmax has read before it stores the first P chunk, so the load
+// of scores 64-127 can still be in flight while P of keys 0-63 is stored, and
+// scores 64-127 stay intact in tensor memory until the next S.
+constexpr uint32_t kPHi = 0;   // P (hi) columns inside an S buffer
+constexpr uint32_t kPLo = 64;  // P (lo) columns inside an S buffer
 
 // Register budget per warpgroup after the split (launch: 512 x 128 = 65536).
-constexpr uint32_t kRegSoftmax = 168;
-constexpr uint32_t kRegEpilogue = 80;
-constexpr uint32_t kRegProducer = 88;
+// The softmax warpgroups hold a 128-score row each; 184 keeps their loop
+// almost free of spills (168 spilled ~76 bytes per thread, measured with
+// -Xptxas -v), paid for by the epilogue and producer warpgroups.
+#ifndef PMKL_PP_REG_SOFTMAX
+#define PMKL_PP_REG_SOFTMAX 184
+#define PMKL_PP_REG_EPILOGUE 64
+#define PMKL_PP_REG_PRODUCER 80
+#endif
+constexpr uint32_t kRegSoftmax = PMKL_PP_REG_SOFTMAX;
+constexpr uint32_t kRegEpilogue = PMKL_PP_REG_EPILOGUE;
+constexpr uint32_t kRegProducer = PMKL_PP_REG_PRODUCER;
 static_assert(128 * (2 * kRegSoftmax + kRegEpilogue + kRegProducer) <= 65536, "register split exceeds the pool");
 constexpr int kLaunchRegs = 128;
 
@@ -161,11 +176,14 @@ __device__ __forceinline__ float2 exp2_poly(float2 x) {
 
 // p = 2^(s * c2 - mref) for one 128-key score row, packed to 16-bit pairs and
 // stored into the P (hi) columns of the row's S buffer (and, with HILO, the
-// rounding remainder into the P (lo) columns).  In each 32-key chunk the first
-// NPOLY pairs go through exp2_poly, the rest through ex2.approx.  Returns the
-// fp32 row sum.
+// rounding remainder into the P (lo) columns).  With `poly`, the first NPOLY
+// pairs of each 32-key chunk go through exp2_poly, the rest through
+// ex2.approx.  Returns the fp32 row sum.  The kernel calls the HILO form (rare:
+// tiles whose rows see at most 128 keys) and the plain form from one place
+// each, so that only one copy of the hot loop competes for the instruction
+// cache with the MMA-issuing warp.
 template <bool BF16, bool HILO, int NPOLY>
-__device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2, float mref, uint32_t sa) {
+__device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2, float mref, uint32_t sa, bool poly) {
     using namespace ptx;
     float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     const float2 c22 = make_float2(c2, c2);
@@ -177,7 +195,8 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2,
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const float2 a = fma2(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), c22, nm2);
-            const float2 e = (i < NPOLY) ? exp2_poly(a) : make_float2(ex2_approx(a.x), ex2_approx(a.y));
+            const float2 e =
+                (!HILO && i < NPOLY && poly) ? exp2_poly(a) : make_float2(ex2_approx(a.x), ex2_approx(a.y));
             rs2[i & 3] = add2(rs2[i & 3], e);
             ph[i] = pack2<BF16>(e.x, e.y);
             if constexpr (HILO) {
@@ -191,6 +210,33 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2,
     }
     const float2 rr = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
     return rr.x + rr.y;
+}
+
+// The speculative form used after a row's first key tile: exps of the 32-key
+// chunks [C0, C1) against a reference taken from earlier tiles, P stored as
+// above, and (TRACK) the row maximum of these scores gathered on the side in
+// four running maxima, so that the maximum is off the path from S to P.
+// Returns the partial row sum as a pair.
+template <bool BF16, int NPOLY, int C0, int C1, bool TRACK>
+__device__ __forceinline__ float2 exp_chunks(const float (&s)[128], float2 c22, float2 nm2, uint32_t sa, bool poly,
+                                             float (&mx)[4]) {
+    using namespace ptx;
+    float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+    for (int c0 = C0; c0 < C1; c0 += 32) {
+        uint32_t ph[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float s0 = s[c0 + 2 * i], s1 = s[c0 + 2 * i + 1];
+            if constexpr (TRACK) mx[i & 3] = fmax3(mx[i & 3], s0, s1);
+            const float2 a = fma2(make_float2(s0, s1), c22, nm2);
+            const float2 e = (i < NPOLY && poly) ? exp2_poly(a) : make_float2(ex2_approx(a.x), ex2_approx(a.y));
+            rs2[i & 1] = add2(rs2[i & 1], e);
+            ph[i] = pack2<BF16>(e.x, e.y);
+        }
+        tmem_st16(sa + kPHi + c0 / 2, ph);
+    }
+    return add2(rs2[0], rs2[1]);
 }
 
 // Pairs per 32-key chunk whose exp2 runs on the FMA pipe (0..16); the rest
@@ -276,7 +322,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tm_q);
             tma_prefetch_desc(&tm_k);
             tma_prefetch_desc(&tm_v);
-            int qc[2] = {0, 0};
+            // Per-tile counters are separate scalars (not arrays indexed by a
+            // run-time tile number), so that they stay in registers.
+            uint32_t qc0 = 0, qc1 = 0;
             int kvc = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
@@ -284,15 +332,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int bb = w.bh / p.H;
                 const int hh = w.bh - bb * p.H;
                 const int hkv = hh / p.kv_group;
-                for (int x = 0; x < 2 && ok; ++x) {
-                    if (!w.act[x]) continue;
-                    if (qc[x] > 0 && !(ok = mbar_wait(&q_empty[x], (qc[x] - 1) & 1, abort_flag))) break;
+                auto load_q = [&](const int x, uint32_t &qcx) {
+                    if (!ok) return;
+                    if (qcx > 0 && !(ok = mbar_wait(&q_empty[x], (qcx - 1) & 1, abort_flag))) return;
                     mbar_arrive_expect_tx(&q_full[x], TILE);
+#pragma unroll
                     for (int b = 0; b < C::kBoxes; ++b)
                         tma_load_4d(sQ + x * TILE + b * kBoxBytes, &tm_q, &q_full[x], b * kBoxCols, w.row0 + 128 * x,
                                     hh, bb);
-                    ++qc[x];
-                }
+                    ++qcx;
+                };
+                if (w.act[0]) load_q(0, qc0);
+                if (w.act[1]) load_q(1, qc1);
                 for (int j = 0; ok && j < w.n_max; ++j) {
                     for (int kv = 0; kv < 2; ++kv) {
                         const int s = kvc % NS;
@@ -310,65 +361,77 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Let issued copies land before shared memory is released.
                 volatile int never = 0;
                 for (int i = max(0, kvc - NS); i < kvc; ++i) mbar_wait(&kv_full[i % NS], (i / NS) & 1, &never);
-                for (int x = 0; x < 2; ++x)
-                    if (qc[x] > 0) mbar_wait(&q_full[x], (qc[x] - 1) & 1, &never);
+                if (qc0 > 0) mbar_wait(&q_full[0], (qc0 - 1) & 1, &never);
+                if (qc1 > 0) mbar_wait(&q_full[1], (qc1 - 1) & 1, &never);
             }
         } else if (!skip && warp == kWarpMma && lane == 0) {
             // ------------------------------------------------------------ MMA issuer
             constexpr uint32_t kIdescS = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
             constexpr uint32_t kIdescO = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
-            int qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+            uint32_t qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0, oc0 = 0, oc1 = 0;
             int kvc = 0;
             bool ok = true;
             // Descriptors are built once; every operand slice is then the base
-            // descriptor plus a constant added to its 14-bit start-address field
-            // (addresses stay below 256 KB, so the field never carries over).
+            // descriptor's low word plus a constant added to its 14-bit
+            // start-address field (addresses stay below 256 KB, so the field
+            // never carries into the high word).
             const uint64_t dq0 = smem_desc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t dk0 = smem_desc_sw128(smem_u32(sRing), 16, 1024);         // K view of stage 0
             const uint64_t dv0 = smem_desc_sw128(smem_u32(sRing), kBoxBytes, 1024);  // V view of stage 0
+            const uint32_t q_lo = static_cast<uint32_t>(dq0), qk_hi = static_cast<uint32_t>(dq0 >> 32);
+            const uint32_t k_lo = static_cast<uint32_t>(dk0);
+            const uint32_t v_lo = static_cast<uint32_t>(dv0), v_hi = static_cast<uint32_t>(dv0 >> 32);
             auto issue_s = [&](int x, int stage) {
-                const uint64_t a0 = dq0 + static_cast<uint64_t>(x * (TILE >> 4));
-                const uint64_t b0 = dk0 + static_cast<uint64_t>(stage * (TILE >> 4));
+                const uint32_t a0 = q_lo + static_cast<uint32_t>(x * (TILE >> 4));
+                const uint32_t b0 = k_lo + static_cast<uint32_t>(stage * (TILE >> 4));
                 const uint32_t d = tmem + col_s(x);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4);
-                    mma_ss(d, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
+                    const uint32_t off = static_cast<uint32_t>(((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4);
+                    mma_ss_h(d, a0 + off, qk_hi, b0 + off, qk_hi, kIdescS, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&s_full[x]);
             };
             auto issue_pv = [&](int x, int stage, bool first, bool hilo) {
-                const uint64_t b0 = dv0 + static_cast<uint64_t>(stage * (TILE >> 4));
+                const uint32_t b0 = v_lo + static_cast<uint32_t>(stage * (TILE >> 4));
                 const uint32_t d = tmem + col_o(x);
                 const uint32_t a = tmem + col_s(x);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(d, a + kPHi + kk * 8, b0 + static_cast<uint64_t>(kk * 128), kIdescO,
-                           (!first || kk > 0) ? 1u : 0u);
+                    mma_ts_h(d, a + kPHi + kk * 8, b0 + static_cast<uint32_t>(kk * 128), v_hi, kIdescO,
+                             (!first || kk > 0) ? 1u : 0u);
                 if (hilo) {
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk)
-                        mma_ts(d, a + kPLo + kk * 8, b0 + static_cast<uint64_t>(kk * 128), kIdescO, 1u);
+                        mma_ts_h(d, a + kPLo + kk * 8, b0 + static_cast<uint32_t>(kk * 128), v_hi, kIdescO, 1u);
                 }
             };
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
                 const Unit w = decode(p, u);
-                for (int x = 0; x < 2 && ok; ++x)
-                    if (w.act[x]) {
-                        ok = mbar_wait(&q_full[x], qc[x] & 1, abort_flag);
-                        ++qc[x];
-                    }
+                const int n0 = w.n[0], n1 = w.n[1];
+                const bool hl0 = w.hilo[0], hl1 = w.hilo[1];
+                if (w.act[0]) {
+                    ok = mbar_wait(&q_full[0], qc0 & 1, abort_flag);
+                    ++qc0;
+                }
+                if (ok && w.act[1]) {
+                    ok = mbar_wait(&q_full[1], qc1 & 1, abort_flag);
+                    ++qc1;
+                }
                 if (!ok) break;
                 // K_0 -> S_A(0), S_B(0)
                 int sK = kvc % NS;
                 if (!(ok = mbar_wait(&kv_full[sK], (kvc / NS) & 1, abort_flag))) break;
                 ++kvc;
                 tc_fence_after();
-                for (int x = 0; x < 2; ++x)
-                    if (w.act[x]) {
-                        issue_s(x, sK);
-                        if (w.n[x] == 1) mma_commit(&q_empty[x]);
-                    }
+                if (w.act[0]) {
+                    issue_s(0, sK);
+                    if (n0 == 1) mma_commit(&q_empty[0]);
+                }
+                if (w.act[1]) {
+                    issue_s(1, sK);
+                    if (n1 == 1) mma_commit(&q_empty[1]);
+                }
                 mma_commit(&kv_empty[sK]);
                 for (int j = 0; ok && j < w.n_max; ++j) {
                     const int sV = kvc % NS;
@@ -381,26 +444,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ++kvc;
                     }
                     bool k_ready = false;
-                    for (int x = 0; x < 2 && ok; ++x) {
-                        if (j >= w.n[x]) continue;
-                        if (!(ok = mbar_wait(&p_full[x], pc[x] & 1, abort_flag))) break;
-                        ++pc[x];
-                        if (j == 0 && oc[x] > 0 && !(ok = mbar_wait(&o_empty[x], (oc[x] - 1) & 1, abort_flag))) break;
+                    auto tile = [&](const int x, const int nx, const bool hlx, uint32_t &pcx, uint32_t &ocx) {
+                        if (!ok || j >= nx) return;
+                        if (!(ok = mbar_wait(&p_full[x], pcx & 1, abort_flag))) return;
+                        ++pcx;
+                        if (j == 0 && ocx > 0 && !(ok = mbar_wait(&o_empty[x], (ocx - 1) & 1, abort_flag))) return;
                         tc_fence_after();
-                        issue_pv(x, sV, j == 0, w.hilo[x]);
-                        if (j + 1 < w.n[x]) {
+                        issue_pv(x, sV, j == 0, hlx);
+                        if (j + 1 < nx) {
                             if (!k_ready) {
-                                if (!(ok = mbar_wait(&kv_full[sK], (kvc_next / NS) & 1, abort_flag))) break;
+                                if (!(ok = mbar_wait(&kv_full[sK], (kvc_next / NS) & 1, abort_flag))) return;
                                 k_ready = true;
                                 tc_fence_after();
                             }
                             issue_s(x, sK);
-                            if (j + 2 == w.n[x]) mma_commit(&q_empty[x]);
+                            if (j + 2 == nx) mma_commit(&q_empty[x]);
                         } else {
                             mma_commit(&o_full[x]);
-                            ++oc[x];
+                            ++ocx;
                         }
-                    }
+                    };
+                    tile(0, n0, hl0, pc0, oc0);
+                    tile(1, n1, hl1, pc1, oc1);
                     if (!ok) break;
                     mma_commit(&kv_empty[sV]);
                     if (has_next) mma_commit(&kv_empty[sK]);
@@ -424,69 +489,114 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
                 const Unit w = decode(p, u);
-                if (!w.act[x]) continue;
+                // This warpgroup's tile, picked by value (no run-time array index).
+                const bool actx = x ? w.act[1] : w.act[0];
+                const int nx = x ? w.n[1] : w.n[0];
+                const bool hilox = x ? w.hilo[1] : w.hilo[0];
+                if (!actx) continue;
                 const int row = w.row0 + 128 * x + r_local;
                 float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
-                for (int j = 0; j < w.n[x]; ++j) {
-                    if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
-                    ++sc;
-                    tc_fence_after();
-                    float s[128];
+                for (int j = 0; j < nx; ++j) {
                     const int kbase = j * 128;
                     int lim = p.S - kbase;
                     if (p.causal) lim = min(lim, row - kbase + 1);
                     const bool masked = __any_sync(0xffffffffu, lim < 128);
-                    float mx8[8];
-                    {
-                        // Two halves: the max of the first overlaps the load of the second.
-                        uint32_t *sr = reinterpret_cast<uint32_t *>(s);
+                    float s[128];
+                    uint32_t *sr = reinterpret_cast<uint32_t *>(s);
+                    auto mask_half = [&](const int h) {
+                        if (masked) {
+#pragma unroll
+                            for (int c = 64 * h; c < 64 * h + 64; ++c)
+                                if (c >= lim) s[c] = -INFINITY;
+                        }
+                    };
+                    float m_new, fac, rsum;
+                    bool any_fac;
+                    if (j == 0) {
+                        // First key tile of the row: the maximum comes first.
+                        if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
+                        ++sc;
+                        tc_fence_after();
+                        float mx8[8];
                         tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
                         tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
                         tmem_wait_ld();
                         tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
                         tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
-                        if (masked) {
+                        mask_half(0);
 #pragma unroll
-                            for (int c = 0; c < 64; ++c)
-                                if (c >= lim) s[c] = -INFINITY;
-                        }
+                        for (int t = 0; t < 8; ++t) mx8[t] = fmax3(s[t], s[t + 8], s[t + 16]);
 #pragma unroll
-                        for (int t = 0; t < 8; ++t) mx8[t] = s[t];
+                        for (int t = 0; t < 8; ++t) mx8[t] = fmax3(mx8[t], s[t + 24], s[t + 32]);
 #pragma unroll
-                        for (int c = 8; c < 64; c += 8)
+                        for (int t = 0; t < 8; ++t) mx8[t] = fmax3(mx8[t], s[t + 40], s[t + 48]);
 #pragma unroll
-                            for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[c + t]);
+                        for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[t + 56]);
                         tmem_wait_ld();
-                        if (masked) {
+                        mask_half(1);
 #pragma unroll
-                            for (int c = 64; c < 128; ++c)
-                                if (c >= lim) s[c] = -INFINITY;
+                        for (int c = 64; c < 128; c += 16)
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) mx8[t] = fmax3(mx8[t], s[c + t], s[c + 8 + t]);
+                        m_true = fmaxf(fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), mx8[6]),
+                                       mx8[7]);
+                        m_new = m_true;
+                        const float mref = (m_new == -INFINITY) ? 0.f : m_new * c2;
+                        if (hilox)
+                            rsum = exp_pack_store<BF16, true, 0>(s, c2, mref, sa, false);
+                        else
+                            rsum = exp_pack_store<BF16, false, NPOLY>(s, c2, mref, sa, !masked);
+                        fac = 0.f;  // l and O hold nothing yet
+                        any_fac = false;
+                    } else {
+                        // Later key tiles: the exps run against a reference taken
+                        // from earlier tiles (known before S arrives) while this
+                        // tile's maximum is gathered alongside.  A reference more
+                        // than 2^8 below the running maximum is moved up first.
+                        // A tile whose own maximum is more than 2^kSpec above the
+                        // reference (P could then overflow the 16-bit type, or
+                        // lose the row's scale) is redone against its maximum.
+                        m_new = ((m_true - m_used) * c2 > 8.0f) ? m_true : m_used;
+                        const float2 c22 = make_float2(c2, c2);
+                        float2 nm2 = make_float2(-m_new * c2, -m_new * c2);
+                        if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
+                        ++sc;
+                        tc_fence_after();
+                        tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                        tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                        tmem_wait_ld();
+                        tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+                        tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+                        mask_half(0);
+                        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                        float2 r = exp_chunks<BF16, NPOLY, 0, 64, true>(s, c22, nm2, sa, !masked, mx);
+                        tmem_wait_ld();
+                        mask_half(1);
+                        r = add2(r, exp_chunks<BF16, NPOLY, 64, 128, true>(s, c22, nm2, sa, !masked, mx));
+                        m_true = fmaxf(m_true, fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]));
+                        constexpr float kSpec = BF16 ? 30.0f : 15.0f;
+                        const bool redo = (m_true - m_new) * c2 > kSpec;
+                        if (__any_sync(0xffffffffu, redo)) {
+                            // Rare: scores 64-127 are reloaded (P went to the
+                            // columns of scores 0-63), scores 0-63 are still in
+                            // registers.
+                            tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+                            tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+                            tmem_wait_ld();
+                            mask_half(1);
+                            if (redo) m_new = m_true;
+                            nm2 = make_float2(-m_new * c2, -m_new * c2);
+                            tmem_wait_st();
+                            float unused[4];
+                            r = exp_chunks<BF16, 0, 0, 128, false>(s, c22, nm2, sa, false, unused);
                         }
-#pragma unroll
-                        for (int c = 64; c < 128; c += 8)
-#pragma unroll
-                            for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[c + t]);
+                        rsum = r.x + r.y;
+                        fac = (m_new == m_used) ? 1.f : ex2_approx((m_used - m_new) * c2);
+                        any_fac = __any_sync(0xffffffffu, m_new != m_used);
                     }
-                    const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-                    m_true = fmaxf(m_true, mx);
-                    const bool resc =
-                        (m_used == -INFINITY) ? (m_true != -INFINITY) : ((m_true - m_used) * c2 > 8.0f);
-                    const bool any_resc = __any_sync(0xffffffffu, resc);
-                    const float m_new = resc ? m_true : m_used;
-                    float fac = 1.f;
-                    if (any_resc) fac = resc ? ((m_used == -INFINITY) ? 0.f : ex2_approx((m_used - m_new) * c2)) : 1.f;
-                    const float mref = (m_new == -INFINITY) ? 0.f : m_new * c2;
-                    float rsum;
-                    if (w.hilo[x])
-                        rsum = exp_pack_store<BF16, true, 0>(s, c2, mref, sa);
-                    else if (masked)
-                        rsum = exp_pack_store<BF16, false, 0>(s, c2, mref, sa);
-                    else
-                        rsum = exp_pack_store<BF16, false, NPOLY>(s, c2, mref, sa);
                     // O_X is idle here: S_X(j) was issued after PV_X(j-1), and
                     // its commit covers every earlier MMA.
-                    if (j > 0 && any_resc) {
+                    if (any_fac) {
 #pragma unroll
                         for (int cc = 0; cc < D / 32; ++cc) {
                             uint32_t o[32];
@@ -523,16 +633,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
             const bool lead = (warp == 8 && lane == 0);
             const float c2 = p.scale_log2;
-            int oc[2] = {0, 0};
+            uint32_t oc0 = 0, oc1 = 0;
             int nb = 0;  // staging boxes used so far
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
                 const Unit w = decode(p, u);
                 for (int x = 0; x < 2 && ok; ++x) {
-                    if (!w.act[x]) continue;
-                    if (!(ok = mbar_wait_warp(&o_full[x], oc[x] & 1, abort_flag))) break;
-                    if (!(ok = mbar_wait_warp(&st_full[x], oc[x] & 1, abort_flag))) break;
-                    ++oc[x];
+                    if (!(x ? w.act[1] : w.act[0])) continue;
+                    const uint32_t ocx = x ? oc1 : oc0;
+                    if (!(ok = mbar_wait_warp(&o_full[x], ocx & 1, abort_flag))) break;
+                    if (!(ok = mbar_wait_warp(&st_full[x], ocx & 1, abort_flag))) break;
+                    if (x) ++oc1; else ++oc0;
                     tc_fence_after();
                     const float m_used = sStats[(x * 3 + 0) * 128 + r_local];
                     const float m_true = sStats[(x * 3 + 1) * 128 + r_local];
