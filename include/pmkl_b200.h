@@ -53,8 +53,6 @@ typedef enum pmkl_attention_kernel {
     PMKL_ATTN_SIMT = 1,    /* generic CUDA-core kernel: any dtype, head size 1..256 */
     PMKL_ATTN_TCGEN05 = 2, /* tensor-core kernel: fp16/bf16, head size 64 or 128 */
     PMKL_ATTN_TCGEN05_SIMPLE = 3, /* one query tile per CTA, non-persistent (comparison only) */
-    PMKL_ATTN_TCGEN05_KV64 = 4,   /* persistent tensor-core kernel with 64-key tiles and double-buffered
-                                     scores (forward only) */
 } pmkl_attention_kernel;
 
 /*

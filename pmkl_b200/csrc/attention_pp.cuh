@@ -245,22 +245,6 @@ __device__ __forceinline__ float2 exp_chunks(const float (&s)[128], float2 c22, 
 #define PMKL_PP_NPOLY 0
 #endif
 
-// Which waits on the per-key-tile chain poll instead of parking the thread:
-// bit 0 the MMA issuer's wait for P, bit 1 the softmax's wait for S.  A
-// build-time knob, tuned on B200.
-#ifndef PMKL_PP_SPIN
-#define PMKL_PP_SPIN 0
-#endif
-
-__device__ __forceinline__ bool wait_p_ready(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    return (PMKL_PP_SPIN & 1) ? ptx::mbar_wait_spin(bar, parity, abort_flag) : ptx::mbar_wait(bar, parity, abort_flag);
-}
-
-__device__ __forceinline__ bool wait_s_ready(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    return (PMKL_PP_SPIN & 2) ? ptx::mbar_wait_spin_warp(bar, parity, abort_flag)
-                              : ptx::mbar_wait_warp(bar, parity, abort_flag);
-}
-
 // DELTA: the backward's instantiation, writing the row statistics (b, delta)
 // instead of O, m, l (DeltaParams).
 template <int D, bool BF16, int NPOLY = PMKL_PP_NPOLY, bool DELTA = false>
@@ -462,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bool k_ready = false;
                     auto tile = [&](const int x, const int nx, const bool hlx, uint32_t &pcx, uint32_t &ocx) {
                         if (!ok || j >= nx) return;
-                        if (!(ok = wait_p_ready(&p_full[x], pcx & 1, abort_flag))) return;
+                        if (!(ok = mbar_wait(&p_full[x], pcx & 1, abort_flag))) return;
                         ++pcx;
                         if (j == 0 && ocx > 0 && !(ok = mbar_wait(&o_empty[x], (ocx - 1) & 1, abort_flag))) return;
                         tc_fence_after();
@@ -530,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bool any_fac;
                     if (j == 0) {
                         // First key tile of the row: the maximum comes first.
-                        if (!(ok = wait_s_ready(&s_full[x], sc & 1, abort_flag))) break;
+                        if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
                         ++sc;
                         tc_fence_after();
                         float mx8[8];
@@ -575,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         m_new = ((m_true - m_used) * c2 > 8.0f) ? m_true : m_used;
                         const float2 c22 = make_float2(c2, c2);
                         float2 nm2 = make_float2(-m_new * c2, -m_new * c2);
-                        if (!(ok = wait_s_ready(&s_full[x], sc & 1, abort_flag))) break;
+                        if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
                         ++sc;
                         tc_fence_after();
                         tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));

@@ -18,7 +18,6 @@
 #include "attention_bwd.cuh"
 #include "attention_bwd_simt.cuh"
 #include "attention_simt.cuh"
-#include "attention_kv64.cuh"
 #include "attention_pp.cuh"
 #include "attention_tc.cuh"
 #include "common.cuh"
@@ -118,10 +117,10 @@ bool make_tile_map(CUtensorMap *map, const void *base, int dtype, int cols, int 
 
 // [batch][heads][rows][cols] 16-bit tensor with element strides st = (batch,
 // head, row) and contiguous columns, viewed as 4-D {cols, rows, heads, batch}
-// for box_rows x 64-column boxes with the 128-byte swizzle.  A dimension of
+// for 128-row x 64-column boxes with the 128-byte swizzle.  A dimension of
 // extent 1 is never stepped, so its stride is replaced by a valid one.
 bool make_tile_map_4d(CUtensorMap *map, const void *base, int dtype, int cols, int rows, int heads, int batch,
-                      const long long (&st)[3], unsigned box_rows = 128u) {
+                      const long long (&st)[3]) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const CUtensorMapDataType dt =
@@ -133,7 +132,7 @@ bool make_tile_map_4d(CUtensorMap *map, const void *base, int dtype, int cols, i
     const cuuint64_t dims[4] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
                                 static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
     const cuuint64_t strides[3] = {row_b, head_b, batch_b};
-    const cuuint32_t box[4] = {static_cast<cuuint32_t>(tc::kBoxCols), static_cast<cuuint32_t>(box_rows), 1u, 1u};
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(tc::kBoxCols), 128u, 1u, 1u};
     const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
     return enc(map, dt, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -198,26 +197,15 @@ int sm_count() {
     return n;
 }
 
-// The persistent kernels: the ping-pong kernel with 128-key tiles
-// (attention_pp.cuh) and the kernel with 64-key tiles and double-buffered
-// scores (attention_kv64.cuh).  Both take the same parameters.
-template <int D, bool BF16, bool DELTA, bool KV64>
-auto persistent_kernel() {
-    if constexpr (KV64)
-        return kv64::attn_fwd_kv64_kernel<D, BF16, DELTA>;
-    else
-        return pp::attn_fwd_pp_kernel<D, BF16, PMKL_PP_NPOLY, DELTA>;
-}
-
-// The persistent kernels re-split their registers between warpgroups with
+// The persistent kernel re-splits its registers between warpgroups with
 // setmaxnreg; the split only fits when the kernel was built with exactly
 // pp::kLaunchRegs registers per thread.  Checked once per process.
-template <int D, bool BF16, bool DELTA = false, bool KV64 = false>
+template <int D, bool BF16, bool DELTA = false>
 bool pp_launchable() {
     static int ok = -1;
     if (ok < 0) {
         cudaFuncAttributes attr;
-        ok = (cudaFuncGetAttributes(&attr, persistent_kernel<D, BF16, DELTA, KV64>()) == cudaSuccess &&
+        ok = (cudaFuncGetAttributes(&attr, pp::attn_fwd_pp_kernel<D, BF16, PMKL_PP_NPOLY, DELTA>) == cudaSuccess &&
               attr.numRegs == pp::kLaunchRegs)
                  ? 1
                  : 0;
@@ -236,22 +224,21 @@ struct DeltaArgs {
     int S_pad;
 };
 
-template <int D, bool BF16, bool KV64 = false>
+template <int D, bool BF16>
 int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int BH, int causal,
               float scale, int dtype, int out_dtype, const AttnLayout &lay, cudaStream_t stream,
               const DeltaArgs *delta = nullptr) {
-    constexpr int kSmem = KV64 ? kv64::Cfg<D>::kSmemBytes : pp::Cfg<D>::kSmemBytes;
-    constexpr unsigned kKVRows = KV64 ? kv64::kBN : 128u;  // rows per K / V box
+    using C = pp::Cfg<D>;
     static std::once_flag smem_once[kMaxDevices];
     static std::once_flag smem_once_delta[kMaxDevices];
-    auto kernel = delta ? persistent_kernel<D, BF16, true, KV64>() : persistent_kernel<D, BF16, false, KV64>();
-    if (!ensure_smem(kernel, kSmem, delta ? smem_once_delta : smem_once)) return PMKL_ERR_LAUNCH;
+    auto kernel = delta ? pp::attn_fwd_pp_kernel<D, BF16, PMKL_PP_NPOLY, true> : pp::attn_fwd_pp_kernel<D, BF16>;
+    if (!ensure_smem(kernel, C::kSmemBytes, delta ? smem_once_delta : smem_once)) return PMKL_ERR_LAUNCH;
     CUtensorMap tq, tk, tv, to;
     const bool o16 = out_dtype != PMKL_DTYPE_F32;
     const int B = BH / lay.H, Hkv = lay.H / lay.kv_group;
     if (!make_tile_map_4d(&tq, q, dtype, D, S, lay.H, B, lay.q) ||
-        !make_tile_map_4d(&tk, k, dtype, D, S, Hkv, B, lay.k, kKVRows) ||
-        !make_tile_map_4d(&tv, v, dtype, D, S, Hkv, B, lay.v, kKVRows) ||
+        !make_tile_map_4d(&tk, k, dtype, D, S, Hkv, B, lay.k) ||
+        !make_tile_map_4d(&tv, v, dtype, D, S, Hkv, B, lay.v) ||
         !make_tile_map_4d(&to, o16 ? o : q, dtype, D, S, lay.H, B, o16 ? lay.o : lay.q))
         return PMKL_ERR_LAUNCH;
     pp::Params p;
@@ -284,7 +271,7 @@ int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, voi
     pp::DeltaParams dp{};
     if (delta) dp = pp::DeltaParams{delta->S_pad, delta->dout, delta->m_given, delta->l_given, delta->rowstat};
     const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
-    kernel<<<grid, pp::kThreads, kSmem, stream>>>(tq, tk, tv, to, p, dp);
+    kernel<<<grid, pp::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, p, dp);
     return launch_status();
 }
 
@@ -341,28 +328,15 @@ int select_kernel(const void *q, const void *k, const void *v, const void *o, in
     const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype, lay);
     // The one-tile kernel reads contiguous [B*H, S, D] tensors only.
     const bool simple_ok = tc_ok && layout_contiguous(lay, S, hidden);
-    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE || kernel == PMKL_ATTN_TCGEN05_KV64) &&
-        !tc_ok)
-        return PMKL_ERR_UNSUPPORTED;
+    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
     if (kernel == PMKL_ATTN_TCGEN05_SIMPLE && !simple_ok) return PMKL_ERR_UNSUPPORTED;
     if (kernel == PMKL_ATTN_SIMT || !tc_ok) return PMKL_ATTN_SIMT;
     if (kernel == PMKL_ATTN_TCGEN05_SIMPLE) return PMKL_ATTN_TCGEN05_SIMPLE;
     const bool bf = dtype == PMKL_DTYPE_BF16;
-    if (kernel == PMKL_ATTN_TCGEN05_KV64) {
-        const bool kv64_ready =
-            hidden == 64 ? (bf ? pp_launchable<64, true, false, true>() : pp_launchable<64, false, false, true>())
-                         : (bf ? pp_launchable<128, true, false, true>() : pp_launchable<128, false, false, true>());
-        return kv64_ready ? static_cast<int>(PMKL_ATTN_TCGEN05_KV64) : static_cast<int>(PMKL_ERR_UNSUPPORTED);
-    }
     const bool ready = hidden == 64 ? (bf ? pp_launchable<64, true>() : pp_launchable<64, false>())
                                     : (bf ? pp_launchable<128, true>() : pp_launchable<128, false>());
     if (ready) return PMKL_ATTN_TCGEN05;
     return simple_ok ? PMKL_ATTN_TCGEN05_SIMPLE : PMKL_ATTN_SIMT;
-}
-
-bool attn_kernel_valid(int kernel) {
-    return kernel == PMKL_ATTN_AUTO || kernel == PMKL_ATTN_SIMT || kernel == PMKL_ATTN_TCGEN05 ||
-           kernel == PMKL_ATTN_TCGEN05_SIMPLE || kernel == PMKL_ATTN_TCGEN05_KV64;
 }
 
 int attention_impl(const void *q, const void *k, const void *v, void *o, void *m, void *l, int batch, int heads,
@@ -371,7 +345,9 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
     if (out_dtype != dtype && out_dtype != PMKL_DTYPE_F32) return PMKL_ERR_INVALID_DTYPE;
-    if (!attn_kernel_valid(kernel)) return PMKL_ERR_UNSUPPORTED;
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
+        return PMKL_ERR_UNSUPPORTED;
     const long long BH = static_cast<long long>(batch) * heads;
     if (BH == 0 || seq == 0 || hidden == 0) return PMKL_OK;  // causal_attention.h:270
     if (hidden > 256) return PMKL_ERR_UNSUPPORTED;
@@ -394,18 +370,6 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
         return hidden == 64
                    ? launch_pp<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream)
                    : launch_pp<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream);
-    }
-    if (chosen == PMKL_ATTN_TCGEN05_KV64) {
-        const int bh = static_cast<int>(BH);
-        if (dtype == PMKL_DTYPE_BF16)
-            return hidden == 64 ? launch_pp<64, true, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype,
-                                                            lay, stream)
-                                : launch_pp<128, true, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype,
-                                                             lay, stream);
-        return hidden == 64 ? launch_pp<64, false, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay,
-                                                         stream)
-                            : launch_pp<128, false, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype,
-                                                          lay, stream);
     }
     if (chosen == PMKL_ATTN_TCGEN05_SIMPLE) {
         const int bh = static_cast<int>(BH);
@@ -807,7 +771,9 @@ int pmkl_causal_attention_fwd_strided(const void *q, const void *k, const void *
 int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
                                    int out_dtype, int kernel) {
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
-    if (!attn_kernel_valid(kernel)) return PMKL_ERR_UNSUPPORTED;
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
+        return PMKL_ERR_UNSUPPORTED;
     const int dev_rc = current_device_ok();
     if (dev_rc != PMKL_OK) return dev_rc;
     const AttnLayout lay = contiguous_layout(1, 128, hidden > 0 ? hidden : 1);

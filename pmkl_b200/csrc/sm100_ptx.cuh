@@ -99,44 +99,6 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, v
     return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
-// Non-blocking test of a phase.
-__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Polling form of mbar_wait for waits on a kernel's critical path: the thread
-// is never parked, so it reacts to the phase change within a few cycles, at
-// the price of issue slots.  The abort flag and the deadline are checked
-// every 256 polls, so the wait stays bounded.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    if (mbar_test_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_test_wait(bar, parity)) return true;
-        if ((i & 255u) == 0) {
-            if (*abort_flag) return false;
-            if (globaltimer() - t0 > kWaitTimeoutNs) {
-                *abort_flag = 1;
-                return false;
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ bool mbar_wait_spin_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait_spin(bar, parity, abort_flag);
-    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-}
-
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
