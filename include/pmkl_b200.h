@@ -53,6 +53,8 @@ typedef enum pmkl_attention_kernel {
     PMKL_ATTN_SIMT = 1,    /* generic CUDA-core kernel: any dtype, head size 1..256 */
     PMKL_ATTN_TCGEN05 = 2, /* tensor-core kernel: fp16/bf16, head size 64 or 128 */
     PMKL_ATTN_TCGEN05_SIMPLE = 3, /* one query tile per CTA, non-persistent (comparison only) */
+    PMKL_ATTN_TCGEN05_DB = 4,     /* persistent, one query tile per work unit with double-buffered
+                                     scores and P (forward only) */
 } pmkl_attention_kernel;
 
 /*
