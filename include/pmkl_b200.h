@@ -124,7 +124,8 @@ int pmkl_causal_attention_fwd_strided(const void *q, const void *k, const void *
 
 /* The kernel pmkl_causal_attention_fwd_ex would run for these arguments:
  * PMKL_ATTN_TCGEN05 (the persistent two-tile tensor-core kernel),
- * PMKL_ATTN_TCGEN05_SIMPLE, PMKL_ATTN_SIMT, or a negative pmkl_status.  Needs
+ * PMKL_ATTN_TCGEN05_SIMPLE, PMKL_ATTN_TCGEN05_DB (only when asked for),
+ * PMKL_ATTN_SIMT, or a negative pmkl_status.  Needs
  * a current sm_100 device.  No reference counterpart (diagnostic). */
 int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
                                    int out_dtype, int kernel);
