@@ -19,10 +19,24 @@
 //   * persistent grid (one CTA per SM); a work unit is one 128-row query tile
 //     of one (batch*head) slice, taken round-robin from a list ordered
 //     longest-first inside groups of slices whose K and V fit in L2.
-//   * warp roles (16 warps): WG0 softmax (one thread per query row = tensor-
-//     memory lane); WG1 idle; WG2 epilogue; warp 12 TMA loads (Q double
-//     buffered per unit; K and V through a ring in the order K0, K1, V0, K2,
-//     V1, K3, ...); warp 13 issues tcgen05.mma.
+//   * warp roles (16 warps): WG0 and WG1 run the softmax of the even and the
+//     odd key tiles of the unit (one thread per query row = tensor-memory
+//     lane; thread i of both warpgroups owns row i); WG2 epilogue; warp 12
+//     TMA loads (Q double buffered per unit; K and V through a ring in the
+//     order K0, K1, V0, K2, V1, K3, ...); warp 13 issues tcgen05.mma.
+//   * exp reference.  Both warpgroups add into one O, so every key tile j has
+//     a reference r_j that both can compute without waiting for each other:
+//     r_j = f(r_(j-1), M_(j-2)), where M_k is the row maximum over key tiles
+//     <= k and f moves the reference up to M only when M lies more than 2^8
+//     above it.  After its exps each warpgroup publishes its tile maximum and
+//     final reference r'_j (r_j, or the tile's own maximum when the tile
+//     lies so far above r_j that P could overflow and is redone) in shared
+//     memory slots indexed by the global key-tile number modulo 4; the other
+//     warpgroup reads them one key tile later (for M and for the O rescale
+//     from r'_(j-1) to r'_j, rare).  A writer cannot lap its reader: writing
+//     tile j + 4 needs P.V(j + 2), which the issuer starts only after P(j + 1),
+//     which the reader releases after reading tile j.  Each warpgroup keeps its
+//     row sum at its own last reference; the epilogue combines the two.
 //   * MMA issue per key tile j: P.V(j) (P from buffer j & 1), then S(j+2)
 //     into the S buffer of S(j), which the softmax has finished reading.
 //     Each P.V commits to pv_done[j & 1]; the softmax waits on it before
@@ -52,11 +66,10 @@ __host__ __device__ constexpr uint32_t col_p(int b) { return b ? 448u : 384u; }
 constexpr uint32_t kColO = 256;
 
 // Register budget per warpgroup after the split (launch: 512 x 128 = 65536).
-constexpr uint32_t kRegSoftmax = 240;
-constexpr uint32_t kRegIdle = 24;
+constexpr uint32_t kRegSoftmax = 184;
 constexpr uint32_t kRegEpilogue = 64;
 constexpr uint32_t kRegProducer = 80;
-static_assert(128 * (kRegSoftmax + kRegIdle + kRegEpilogue + kRegProducer) <= 65536, "register split exceeds the pool");
+static_assert(128 * (2 * kRegSoftmax + kRegEpilogue + kRegProducer) <= 65536, "register split exceeds the pool");
 constexpr int kLaunchRegs = 128;
 
 template <int D>
@@ -68,9 +81,10 @@ struct Cfg {
     static constexpr int kOffQ = 0;                       // two Q slots
     static constexpr int kOffStage = 2 * kTile;           // epilogue staging, one 128 x 64 box
     static constexpr int kOffRing = kOffStage + kBoxBytes;
-    static constexpr int kOffStats = kOffRing + kStages * kTile;  // [3][128] {m_used, m_true, l}
-    static constexpr int kOffBars = kOffStats + 3 * 128 * 4;
-    static constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 + 2 + 2 + 1 + 1 + 1 + 1 + 3;
+    static constexpr int kOffStats = kOffRing + kStages * kTile;  // [2 warpgroups][3][128] {ref, max, l}
+    static constexpr int kOffPub = kOffStats + 2 * 3 * 128 * 4;     // [4 slots][2][128] {tile max, ref}
+    static constexpr int kOffBars = kOffPub + 4 * 2 * 128 * 4;
+    static constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 + 2 + 2 + 1 + 1 + 1 + 1 + 3 + 4;
     static constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
     static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -170,7 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *sQ = smem + C::kOffQ;  // [2][TILE]
     uint8_t *sStage = smem + C::kOffStage;
     uint8_t *sRing = smem + C::kOffRing;  // [NS][TILE]
-    float *sStats = reinterpret_cast<float *>(smem + C::kOffStats);  // [3][128]
+    float *sStats = reinterpret_cast<float *>(smem + C::kOffStats);  // [2][3][128]
+    float *sPub = reinterpret_cast<float *>(smem + C::kOffPub);      // [4][2][128]
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kOffBars);
     uint64_t *q_full = bars;            // [2]
     uint64_t *q_empty = bars + 2;       // [2]
@@ -186,7 +201,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *mma_done = st_empty + 1;
     uint64_t *stg_written = mma_done + 1;  // epilogue warps -> store thread
     uint64_t *stg_free = stg_written + 1;  // store thread -> epilogue warps
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(stg_free + 1);
+    uint64_t *pub_full = stg_free + 1;     // [4] publication slots, one writer warpgroup each time
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pub_full + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -207,7 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(o_full, 1);
         mbar_init(o_empty, 4);
-        mbar_init(st_full, 4);
+        mbar_init(st_full, 8);
+        for (int i = 0; i < 4; ++i) mbar_init(&pub_full[i], 4);
         mbar_init(st_empty, 4);
         mbar_init(mma_done, 1);
         mbar_init(stg_written, 4);
@@ -363,23 +380,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             volatile int never = 0;
             mbar_wait(mma_done, 0, &never);
         }
-    } else if (wg == 1) {
-        reg_dealloc<kRegIdle>();
-    } else if (wg == 0) {
+    } else if (wg < 2) {
         reg_alloc<kRegSoftmax>();
         if (!skip) {
-            // ------------------------------------------------------------ softmax
-            const int r_local = warp * 32 + lane;  // == tensor-memory lane
-            const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+            // ------------------------------------------------------------ softmax of key tiles j = x, x + 2, ...
+            const int x = wg;
+            const int r_local = (warp & 3) * 32 + lane;  // == tensor-memory lane
+            const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
             const float c2 = p.scale_log2;
             const float2 c22 = make_float2(c2, c2);
+            // The reference moves up to a lagged maximum only when it lies more than 2^8 above.
+            auto move_ref = [&](float r, float M) { return (M != -INFINITY && M * c2 - r > 8.0f) ? M * c2 : r; };
+            auto publish = [&](int G, float tmax, float rfin) {
+                float *slot = sPub + (G & 3) * 256;
+                slot[r_local] = tmax;
+                slot[128 + r_local] = rfin;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pub_full[G & 3]);
+            };
             int g = 0, uc = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
                 const Unit w = unit_at(p, u);
                 const int row = w.row0 + r_local;
-                float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
-                for (int j = 0; j < w.n; ++j) {
+                float l = 0.f, lref = 0.f;  // this warpgroup's row sum and the reference it is held at
+                float m_own = -INFINITY;    // maximum over this warpgroup's key tiles
+                float Ma = -INFINITY, Mb = -INFINITY;  // M_(j-3), M_(j-2) at the start of own tile j
+                float ra = 0.f;                        // r_(j-2)
+                for (int j = x; j < w.n; j += 2) {
                     const int G = g + j;
                     const int buf = G & 1;
                     const uint32_t sa = lane_base + col_s(buf);
@@ -402,11 +430,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // P buffer `buf` is free once P.V two key tiles back has read it.
                     if (G >= 2 && !(ok = mbar_wait_warp(&pv_done[buf], ((G >> 1) - 1) & 1, abort_flag))) break;
                     tc_fence_after();
-                    float m_new, fac, rsum;
-                    bool any_fac;
+                    float tmax = -INFINITY, rj, rfin, rsum;
+                    float tprev = -INFINITY, rprev = 0.f;  // the other warpgroup's tile j - 1
                     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
                     if (j == 0) {
-                        // First key tile of the row: the maximum comes first.
+                        // First key tile of the unit: the maximum comes first and is
+                        // published at once (the other warpgroup starts from it).
                         tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
                         tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
                         tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
@@ -423,27 +452,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int t = 0; t < 8; ++t) mx8[t] = fmax3(mx8[t], s[c + t], s[c + 8 + t]);
 #pragma unroll
                         for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[120 + t]);
-                        m_true = fmaxf(fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), mx8[6]),
-                                       mx8[7]);
-                        m_new = m_true;
-                        const float mref = (m_new == -INFINITY) ? 0.f : m_new * c2;
-                        const float2 nm2 = make_float2(-mref, -mref);
+                        tmax = fmaxf(fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), mx8[6]),
+                                     mx8[7]);
+                        rj = (tmax == -INFINITY) ? 0.f : tmax * c2;
+                        rfin = rj;
+                        publish(G, tmax, rfin);
+                        const float2 nm2 = make_float2(-rj, -rj);
                         float2 r;
                         if (w.hilo)
                             r = exp_chunks<BF16, true, 0, 128, false>(s, c22, nm2, pa, pl, mx);
                         else
                             r = exp_chunks<BF16, false, 0, 128, false>(s, c22, nm2, pa, pl, mx);
                         rsum = r.x + r.y;
-                        fac = 0.f;  // l and O hold nothing yet
-                        any_fac = false;
                     } else {
-                        // Later key tiles: exps against a reference taken from
-                        // earlier tiles while this tile's maximum is gathered
-                        // alongside.  A reference more than 2^8 below the running
-                        // maximum is moved up first; a tile whose own maximum is
-                        // more than 2^kSpec above the reference is redone.
-                        m_new = ((m_true - m_used) * c2 > 8.0f) ? m_true : m_used;
-                        float2 nm2 = make_float2(-m_new * c2, -m_new * c2);
+                        if (j == 1) {
+                            // r_1 = r_0, the other warpgroup's first reference.
+                            if (!(ok = mbar_wait_warp(&pub_full[(G - 1) & 3], ((G - 1) >> 2) & 1, abort_flag))) break;
+                            tprev = sPub[((G - 1) & 3) * 256 + r_local];
+                            rprev = sPub[((G - 1) & 3) * 256 + 128 + r_local];
+                            rj = rprev;
+                        } else {
+                            rj = move_ref(move_ref(ra, Ma), Mb);  // r_j from r_(j-2) via r_(j-1)
+                        }
+                        float2 nm2 = make_float2(-rj, -rj);
                         tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
                         tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
                         tmem_wait_ld();
@@ -454,36 +485,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tmem_wait_ld();
                         mask_half(1);
                         r = add2(r, exp_chunks<BF16, false, 64, 128, true>(s, c22, nm2, pa, pl, mx));
-                        m_true = fmaxf(m_true, fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]));
+                        tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+                        // A tile whose maximum lies more than 2^kSpec above its reference
+                        // (P could overflow the 16-bit type) is redone against that maximum.
                         constexpr float kSpec = BF16 ? 30.0f : 15.0f;
-                        const bool redo = (m_true - m_new) * c2 > kSpec;
+                        const bool redo = tmax * c2 - rj > kSpec;
+                        rfin = redo ? tmax * c2 : rj;
                         if (__any_sync(0xffffffffu, redo)) {
-                            // Rare: every score is still in registers and in S.
-                            if (redo) m_new = m_true;
-                            nm2 = make_float2(-m_new * c2, -m_new * c2);
+                            nm2 = make_float2(-rfin, -rfin);
                             tmem_wait_st();
                             r = exp_chunks<BF16, false, 0, 128, false>(s, c22, nm2, pa, pl, mx);
                         }
                         rsum = r.x + r.y;
-                        fac = (m_new == m_used) ? 1.f : ex2_approx((m_used - m_new) * c2);
-                        any_fac = __any_sync(0xffffffffu, m_new != m_used);
-                    }
-                    if (any_fac) {
-                        // P.V(j-1) may still be adding into O: wait for it.
-                        if (!(ok = mbar_wait_warp(&pv_done[buf ^ 1], ((G - 1) >> 1) & 1, abort_flag))) break;
-                        tc_fence_after();
+                        publish(G, tmax, rfin);
+                        if (j > 1) {
+                            if (!(ok = mbar_wait_warp(&pub_full[(G - 1) & 3], ((G - 1) >> 2) & 1, abort_flag))) break;
+                            tprev = sPub[((G - 1) & 3) * 256 + r_local];
+                            rprev = sPub[((G - 1) & 3) * 256 + 128 + r_local];
+                        }
+                        // O holds key tiles < j at reference r'_(j-1); bring it to r'_j.
+                        if (__any_sync(0xffffffffu, rprev != rfin)) {
+                            if (!(ok = mbar_wait_warp(&pv_done[buf ^ 1], ((G - 1) >> 1) & 1, abort_flag))) break;
+                            tc_fence_after();
+                            const float fac = (rprev == rfin) ? 1.f : ex2_approx(rprev - rfin);
 #pragma unroll
-                        for (int cc = 0; cc < D / 32; ++cc) {
-                            uint32_t o[32];
-                            tmem_ld32(lane_base + kColO + cc * 32, o);
-                            tmem_wait_ld();
+                            for (int cc = 0; cc < D / 32; ++cc) {
+                                uint32_t o[32];
+                                tmem_ld32(lane_base + kColO + cc * 32, o);
+                                tmem_wait_ld();
 #pragma unroll
-                            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * fac);
-                            tmem_st32(lane_base + kColO + cc * 32, o);
+                                for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * fac);
+                                tmem_st32(lane_base + kColO + cc * 32, o);
+                            }
                         }
                     }
-                    l = l * fac + rsum;
-                    m_used = m_new;
+                    l = (j == x) ? rsum : l * ex2_approx(lref - rfin) + rsum;
+                    lref = rfin;
+                    m_own = fmaxf(m_own, tmax);
+                    const float Mjm1 = fmaxf(Mb, tprev);  // M_(j-1)
+                    Ma = Mjm1;
+                    Mb = fmaxf(Mjm1, tmax);  // M_j
+                    ra = rj;
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
@@ -491,11 +533,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) break;
                 g += w.n;
-                // Row statistics for the epilogue.
+                // Row statistics for the epilogue (a warpgroup without key tiles reports l = 0).
                 if (uc > 0 && !(ok = mbar_wait_warp(st_empty, (uc - 1) & 1, abort_flag))) break;
-                sStats[0 * 128 + r_local] = m_used;
-                sStats[1 * 128 + r_local] = m_true;
-                sStats[2 * 128 + r_local] = l;
+                sStats[(x * 3 + 0) * 128 + r_local] = lref;
+                sStats[(x * 3 + 1) * 128 + r_local] = m_own;
+                sStats[(x * 3 + 2) * 128 + r_local] = (x < w.n) ? l : 0.f;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(st_full);
                 ++uc;
@@ -518,12 +560,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!(ok = mbar_wait_warp(st_full, oc & 1, abort_flag))) break;
                 ++oc;
                 tc_fence_after();
-                const float m_used = sStats[0 * 128 + r_local];
-                const float m_true = sStats[1 * 128 + r_local];
-                const float l = sStats[2 * 128 + r_local];
+                // O is held at the reference of the unit's last key tile.
+                const int xl = (w.n - 1) & 1;
+                const float R = sStats[(xl * 3 + 0) * 128 + r_local];
+                float l = 0.f;
+#pragma unroll
+                for (int xx = 0; xx < 2; ++xx) {
+                    const float lx = sStats[(xx * 3 + 2) * 128 + r_local];
+                    if (lx > 0.f) l += lx * ex2_approx(sStats[(xx * 3 + 0) * 128 + r_local] - R);
+                }
+                const float m_true = fmaxf(sStats[1 * 128 + r_local], sStats[4 * 128 + r_local]);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(st_empty);
                 const float inv_l = 1.f / l;
+                // l at the row maximum m_true (the reference of the m, l outputs).
+                const float l_true = (m_true == -INFINITY) ? 0.f : l * ex2_approx(R - m_true * c2);
                 const int row = w.row0 + r_local;
                 const uint32_t oa = lane_base + kColO;
                 const int bb = w.bh / p.H;
@@ -562,7 +613,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (row < p.S) {
                         const float mg = Elem<T>::to_float(static_cast<const T *>(dpar.m_given)[ridx]);
                         const float lg = Elem<T>::to_float(static_cast<const T *>(dpar.l_given)[ridx]);
-                        const float l_true = (m_true == -INFINITY) ? 0.f : l * ex2_approx((m_used - m_true) * c2);
                         const float f = expf(m_true * p.scale - mg) * (l_true / lg);
                         rs = make_float2(mg * 1.4426950408889634f + log2f(lg), f * dot * inv_l);
                     }
@@ -638,7 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (row < p.S) {
                     const size_t idx = static_cast<size_t>(w.bh) * p.S + row;
                     store_as(p.m_out, idx, p.out_dtype, m_true * p.scale);
-                    store_as(p.l_out, idx, p.out_dtype, (m_true == -INFINITY) ? 0.f : l * ex2_approx((m_used - m_true) * c2));
+                    store_as(p.l_out, idx, p.out_dtype, l_true);
                 }
             }
             if (lead) tma_store_wait0();
