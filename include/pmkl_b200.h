@@ -53,8 +53,6 @@ typedef enum pmkl_attention_kernel {
     PMKL_ATTN_SIMT = 1,    /* generic CUDA-core kernel: any dtype, head size 1..256 */
     PMKL_ATTN_TCGEN05 = 2, /* tensor-core kernel: fp16/bf16, head size 64 or 128 */
     PMKL_ATTN_TCGEN05_SIMPLE = 3, /* one query tile per CTA, non-persistent (comparison only) */
-    PMKL_ATTN_TCGEN05_DB = 4,     /* persistent, one query tile per work unit with double-buffered
-                                     scores and P (forward only) */
 } pmkl_attention_kernel;
 
 /*
@@ -124,8 +122,7 @@ int pmkl_causal_attention_fwd_strided(const void *q, const void *k, const void *
 
 /* The kernel pmkl_causal_attention_fwd_ex would run for these arguments:
  * PMKL_ATTN_TCGEN05 (the persistent two-tile tensor-core kernel),
- * PMKL_ATTN_TCGEN05_SIMPLE, PMKL_ATTN_TCGEN05_DB (only when asked for),
- * PMKL_ATTN_SIMT, or a negative pmkl_status.  Needs
+ * PMKL_ATTN_TCGEN05_SIMPLE, PMKL_ATTN_SIMT, or a negative pmkl_status.  Needs
  * a current sm_100 device.  No reference counterpart (diagnostic). */
 int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
                                    int out_dtype, int kernel);

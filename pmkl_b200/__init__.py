@@ -28,7 +28,7 @@ EXT_DIR = PKG_DIR / "torch_ext" / "_build"
 FUNCTION_DIR = PKG_DIR / "torch_ext"
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
-KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05, KERNEL_TCGEN05_SIMPLE, KERNEL_TCGEN05_DB = 0, 1, 2, 3, 4
+KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
 PMKL_OK = 0
 
 for _p in (EXT_DIR, FUNCTION_DIR):
@@ -159,7 +159,7 @@ def attention_bwd(dout, q, k, v, m, l, dq, dk, dv, is_causal: bool, scale: float
 
 
 KERNEL_NAMES = {KERNEL_SIMT: "attn_fwd_simt_kernel", KERNEL_TCGEN05: "attn_fwd_pp_kernel",
-                KERNEL_TCGEN05_SIMPLE: "attn_fwd_tc_kernel", KERNEL_TCGEN05_DB: "attn_fwd_sd_kernel"}
+                3: "attn_fwd_tc_kernel"}
 
 
 def attention_selected_kernel(q, k, v, o, kernel: int = KERNEL_AUTO) -> int:

@@ -19,7 +19,6 @@
 #include "attention_bwd_simt.cuh"
 #include "attention_simt.cuh"
 #include "attention_pp.cuh"
-#include "attention_sd.cuh"
 #include "attention_tc.cuh"
 #include "common.cuh"
 #include "pmkl_b200.h"
@@ -276,70 +275,6 @@ int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, voi
     return launch_status();
 }
 
-// The one-tile double-buffered kernel (attention_sd.cuh); same register-split
-// requirement as the ping-pong kernel.
-template <int D, bool BF16, bool DELTA = false>
-bool sd_launchable() {
-    static int ok = -1;
-    if (ok < 0) {
-        cudaFuncAttributes attr;
-        ok = (cudaFuncGetAttributes(&attr, sd::attn_fwd_sd_kernel<D, BF16, DELTA>) == cudaSuccess &&
-              attr.numRegs == sd::kLaunchRegs)
-                 ? 1
-                 : 0;
-        cudaGetLastError();
-    }
-    return ok == 1;
-}
-
-template <int D, bool BF16>
-int launch_sd(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int BH, int causal,
-              float scale, int dtype, int out_dtype, const AttnLayout &lay, cudaStream_t stream,
-              const DeltaArgs *delta = nullptr) {
-    using C = sd::Cfg<D>;
-    static std::once_flag smem_once[kMaxDevices];
-    static std::once_flag smem_once_delta[kMaxDevices];
-    auto kernel = delta ? sd::attn_fwd_sd_kernel<D, BF16, true> : sd::attn_fwd_sd_kernel<D, BF16, false>;
-    if (!ensure_smem(kernel, C::kSmemBytes, delta ? smem_once_delta : smem_once)) return PMKL_ERR_LAUNCH;
-    CUtensorMap tq, tk, tv, to;
-    const bool o16 = out_dtype != PMKL_DTYPE_F32;
-    const int B = BH / lay.H, Hkv = lay.H / lay.kv_group;
-    if (!make_tile_map_4d(&tq, q, dtype, D, S, lay.H, B, lay.q) ||
-        !make_tile_map_4d(&tk, k, dtype, D, S, Hkv, B, lay.k) ||
-        !make_tile_map_4d(&tv, v, dtype, D, S, Hkv, B, lay.v) ||
-        !make_tile_map_4d(&to, o16 ? o : q, dtype, D, S, lay.H, B, o16 ? lay.o : lay.q))
-        return PMKL_ERR_LAUNCH;
-    sd::Params p;
-    p.S = S;
-    p.BH = BH;
-    p.H = lay.H;
-    p.kv_group = lay.kv_group;
-    p.o_sb = lay.o[0];
-    p.o_sh = lay.o[1];
-    p.o_ss = lay.o[2];
-    p.n_qt = (S + 127) / 128;
-    const long long units = static_cast<long long>(p.n_qt) * BH;
-    if (units > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
-    p.n_units = static_cast<int>(units);
-    const long long kv_bytes = 2LL * S * D * 2;
-    long long grp = PMKL_PP_GROUP_BYTES / (kv_bytes > 0 ? kv_bytes : 1);
-    if (grp < 1) grp = 1;
-    if (grp > BH) grp = BH;
-    p.group = static_cast<int>(grp);
-    p.causal = causal;
-    p.out_dtype = out_dtype;
-    p.scale = scale;
-    p.scale_log2 = scale * 1.4426950408889634f;
-    p.o_f32 = o;
-    p.m_out = m;
-    p.l_out = l;
-    pp::DeltaParams dp{};
-    if (delta) dp = pp::DeltaParams{delta->S_pad, delta->dout, delta->m_given, delta->l_given, delta->rowstat};
-    const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
-    kernel<<<grid, sd::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, p, dp);
-    return launch_status();
-}
-
 template <typename T, int DMAX>
 int launch_simt_t(const void *q, const void *k, const void *v, void *o, void *m, void *l, int S, int D, int BH,
                   int causal, float scale, int out_dtype, const AttnLayout &lay, cudaStream_t stream) {
@@ -393,27 +328,15 @@ int select_kernel(const void *q, const void *k, const void *v, const void *o, in
     const bool tc_ok = tc_applies(q, k, v, o, hidden, dtype, out_dtype, lay);
     // The one-tile kernel reads contiguous [B*H, S, D] tensors only.
     const bool simple_ok = tc_ok && layout_contiguous(lay, S, hidden);
-    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE || kernel == PMKL_ATTN_TCGEN05_DB) &&
-        !tc_ok)
-        return PMKL_ERR_UNSUPPORTED;
+    if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
     if (kernel == PMKL_ATTN_TCGEN05_SIMPLE && !simple_ok) return PMKL_ERR_UNSUPPORTED;
     if (kernel == PMKL_ATTN_SIMT || !tc_ok) return PMKL_ATTN_SIMT;
     if (kernel == PMKL_ATTN_TCGEN05_SIMPLE) return PMKL_ATTN_TCGEN05_SIMPLE;
     const bool bf = dtype == PMKL_DTYPE_BF16;
-    if (kernel == PMKL_ATTN_TCGEN05_DB) {
-        const bool db_ready = hidden == 64 ? (bf ? sd_launchable<64, true>() : sd_launchable<64, false>())
-                                           : (bf ? sd_launchable<128, true>() : sd_launchable<128, false>());
-        return db_ready ? static_cast<int>(PMKL_ATTN_TCGEN05_DB) : static_cast<int>(PMKL_ERR_UNSUPPORTED);
-    }
     const bool ready = hidden == 64 ? (bf ? pp_launchable<64, true>() : pp_launchable<64, false>())
                                     : (bf ? pp_launchable<128, true>() : pp_launchable<128, false>());
     if (ready) return PMKL_ATTN_TCGEN05;
     return simple_ok ? PMKL_ATTN_TCGEN05_SIMPLE : PMKL_ATTN_SIMT;
-}
-
-bool attn_kernel_valid(int kernel) {
-    return kernel == PMKL_ATTN_AUTO || kernel == PMKL_ATTN_SIMT || kernel == PMKL_ATTN_TCGEN05 ||
-           kernel == PMKL_ATTN_TCGEN05_SIMPLE || kernel == PMKL_ATTN_TCGEN05_DB;
 }
 
 int attention_impl(const void *q, const void *k, const void *v, void *o, void *m, void *l, int batch, int heads,
@@ -422,7 +345,9 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
     if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
     if (out_dtype != dtype && out_dtype != PMKL_DTYPE_F32) return PMKL_ERR_INVALID_DTYPE;
-    if (!attn_kernel_valid(kernel)) return PMKL_ERR_UNSUPPORTED;
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
+        return PMKL_ERR_UNSUPPORTED;
     const long long BH = static_cast<long long>(batch) * heads;
     if (BH == 0 || seq == 0 || hidden == 0) return PMKL_OK;  // causal_attention.h:270
     if (hidden > 256) return PMKL_ERR_UNSUPPORTED;
@@ -445,16 +370,6 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
         return hidden == 64
                    ? launch_pp<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream)
                    : launch_pp<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream);
-    }
-    if (chosen == PMKL_ATTN_TCGEN05_DB) {
-        const int bh = static_cast<int>(BH);
-        if (dtype == PMKL_DTYPE_BF16)
-            return hidden == 64
-                       ? launch_sd<64, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream)
-                       : launch_sd<128, true>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream);
-        return hidden == 64
-                   ? launch_sd<64, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream)
-                   : launch_sd<128, false>(q, k, v, o, m, l, seq, bh, causal, sc, dtype, out_dtype, lay, stream);
     }
     if (chosen == PMKL_ATTN_TCGEN05_SIMPLE) {
         const int bh = static_cast<int>(BH);
@@ -856,7 +771,9 @@ int pmkl_causal_attention_fwd_strided(const void *q, const void *k, const void *
 int pmkl_attention_selected_kernel(const void *q, const void *k, const void *v, const void *o, int hidden, int dtype,
                                    int out_dtype, int kernel) {
     if (!dtype_valid(dtype) || !dtype_valid(out_dtype)) return PMKL_ERR_INVALID_DTYPE;
-    if (!attn_kernel_valid(kernel)) return PMKL_ERR_UNSUPPORTED;
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
+        return PMKL_ERR_UNSUPPORTED;
     const int dev_rc = current_device_ok();
     if (dev_rc != PMKL_OK) return dev_rc;
     const AttnLayout lay = contiguous_layout(1, 128, hidden > 0 ? hidden : 1);

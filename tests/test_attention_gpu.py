@@ -18,11 +18,7 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 TC = pmkl_b200.KERNEL_TCGEN05
-DB = pmkl_b200.KERNEL_TCGEN05_DB
 SIMT = pmkl_b200.KERNEL_SIMT
-# The two persistent tensor-core kernels: two-tile ping-pong, and one tile
-# with double-buffered scores and P.
-TCK = [TC, DB]
 LP = [torch.bfloat16, torch.float16]
 ATTN_F32 = sorted(p.stem for p in GOLDEN.glob("attn_*f32*.npz") if not p.stem.startswith("attn_bwd"))
 
@@ -81,17 +77,16 @@ def test_golden_fp32(name):
     assert_f32_close(np32(o), g["o"], name + " O")
 
 
-@pytest.mark.parametrize("kernel", TCK)
 @pytest.mark.parametrize("dtype", LP)
 @pytest.mark.parametrize("name", [n for n in ATTN_F32 if "d64" in n or "d128" in n])
-def test_golden_inputs_lowp_tc(name, dtype, kernel):
+def test_golden_inputs_lowp_tc(name, dtype):
     """The golden inputs rounded to fp16/bf16 through the tensor-core path."""
     g = load_golden(name)
     q, k, v = (torch.from_numpy(g[x]).to(dtype) for x in ("q", "k", "v"))
     causal = bool(g["causal"])
-    o, m, l = attention_capi(q, k, v, causal, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, causal, kernel=TC)
     check_lp(q, k, v, causal, o, m, l, name)
-    o32, m32, l32 = attention_capi(q, k, v, causal, out_fp32=True, kernel=kernel)
+    o32, m32, l32 = attention_capi(q, k, v, causal, out_fp32=True, kernel=TC)
     check_lp(q, k, v, causal, o32, m32, l32, name + " fp32-out")
 
 
@@ -110,14 +105,13 @@ def test_golden_lowp_fixtures(name):
 EDGE_S = [1, 2, 5, 64, 127, 128, 129, 200, 255, 256, 257, 384, 515]
 
 
-@pytest.mark.parametrize("kernel", TCK)
 @pytest.mark.parametrize("dtype", LP)
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("S", EDGE_S)
-def test_edge_shapes_tc(S, causal, D, dtype, kernel):
+def test_edge_shapes_tc(S, causal, D, dtype):
     q, k, v = seeded_qkv(1, 2, S, D, dtype, seed=S * 7 + D + int(causal))
-    o, m, l = attention_capi(q, k, v, causal, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, causal, kernel=TC)
     check_lp(q, k, v, causal, o, m, l, f"S{S} D{D} causal={causal}")
 
 
@@ -137,24 +131,22 @@ def test_simt_head_sizes(D, causal, dtype):
         check_lp(q, k, v, causal, o, m, l, f"simt D{D}")
 
 
-@pytest.mark.parametrize("kernel", TCK)
-def test_custom_scale(kernel):
+def test_custom_scale():
     q, k, v = seeded_qkv(1, 2, 300, 128, torch.bfloat16, seed=5)
     for sc in (0.05, 0.1):  # score std 0.57 and 1.13
-        o, m, l = attention_capi(q, k, v, True, kernel=kernel, scale=sc)
+        o, m, l = attention_capi(q, k, v, True, kernel=TC, scale=sc)
         ro, rm, rl = oracle.attention_fwd(np32(q), np32(k), np32(v), True, scale=sc)
         assert_lp_close(np32(o), ro, torch.bfloat16, "O")
         assert_lp_close(np32(m), rm, torch.bfloat16, "m")
 
 
-@pytest.mark.parametrize("kernel", TCK)
-def test_peaked_scores_bf16_p_bound(kernel):
+def test_peaked_scores_bf16_p_bound():
     """With very peaked scores (scale 0.3: score std 3.4) a row has only a few
     effective keys even far from the start, and the one rounding of P to bf16
     before P.V (2^-9 relative per weight, as in any flash kernel) shows:
     |O - O_ref| <= 2^-8 * max|v| bounds it (plus the output's half ulp)."""
     q, k, v = seeded_qkv(1, 2, 300, 128, torch.bfloat16, seed=5)
-    o, m, l = attention_capi(q, k, v, True, kernel=kernel, scale=0.3)
+    o, m, l = attention_capi(q, k, v, True, kernel=TC, scale=0.3)
     ro, rm, rl = oracle.attention_fwd(np32(q), np32(k), np32(v), True, scale=0.3)
     got = np32(o).astype(np.float64)
     vmax = float(np.abs(np32(v)).max())
@@ -163,11 +155,10 @@ def test_peaked_scores_bf16_p_bound(kernel):
     assert_lp_close(np32(m), rm, torch.bfloat16, "m")
 
 
-@pytest.mark.parametrize("kernel", TCK)
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("dtype", LP)
-def test_row_max_jumps_after_first_key_tile(causal, D, dtype, kernel):
+def test_row_max_jumps_after_first_key_tile(causal, D, dtype):
     """Keys of the later key tiles are scaled up (x6 for keys 128..255, x12
     beyond), so most rows' maxima jump by far more than 2^8 after the first key
     tile: the kernel's exp reference point must move and O be rescaled.
@@ -176,7 +167,7 @@ def test_row_max_jumps_after_first_key_tile(causal, D, dtype, kernel):
     k = k.clone()
     k[:, :, 128:256] *= 6
     k[:, :, 256:] *= 12
-    o, m, l = attention_capi(q, k, v, causal, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, causal, kernel=TC)
     ro, rm, rl = oracle.attention_fwd(np32(q), np32(k), np32(v), causal)
     got = np32(o).astype(np.float64)
     vmax = float(np.abs(np32(v)).max())
@@ -199,12 +190,11 @@ def test_config1_fp32():
     assert_f32_close(np32(l), rl, "l")
 
 
-@pytest.mark.parametrize("kernel", [0] + TCK)
-def test_config2_fp16(kernel):
+def test_config2_fp16():
     """fp16 B8 H16 S1024 D64 causal.  Every 8th (b, h) slice
     is checked against the full oracle (all rows)."""
     q, k, v = seeded_qkv(8, 16, 1024, 64, torch.float16, seed=12)
-    o, m, l = attention_capi(q, k, v, True, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, True)
     sl = slice(0, None, 8)
     qs, ks, vs = (t.reshape(128, 1, 1024, 64)[sl] for t in (q, k, v))
     check_lp(qs, ks, vs, True, o.reshape(128, 1, 1024, 64)[sl], m.reshape(128, 1, 1024)[sl],
@@ -236,66 +226,60 @@ def sampled_rows_check(q, k, v, causal, o, m, l, n_slices, rows_per_slice, seed)
     assert rel.max() < 2e-3 + 2.0 ** -8
 
 
-@pytest.mark.parametrize("kernel", [0] + TCK)
-def test_config3_bf16_sampled(kernel):
+def test_config3_bf16_sampled():
     """bf16 B16 H32 S4096 D128 causal, N(0,1); the oracle
     on sampled rows (tile boundaries included) of sampled slices."""
     q, k, v = seeded_qkv(16, 32, 4096, 128, torch.bfloat16, seed=13)
-    o, m, l = attention_capi(q, k, v, True, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, True)
     sampled_rows_check(q, k, v, True, o, m, l, n_slices=6, rows_per_slice=20, seed=3)
 
 
-@pytest.mark.parametrize("kernel", [0] + TCK)
-def test_config4_bf16_sampled(kernel):
+def test_config4_bf16_sampled():
     """bf16 B1 H32 S32768 D128 causal, N(0, 0.5^2)."""
     q, k, v = seeded_qkv(1, 32, 32768, 128, torch.bfloat16, seed=14, std=0.5)
-    o, m, l = attention_capi(q, k, v, True, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, True)
     sampled_rows_check(q, k, v, True, o, m, l, n_slices=3, rows_per_slice=8, seed=4)
 
 
 # ------------------------------------------------------------------ size-independent properties
-@pytest.mark.parametrize("kernel", [0] + TCK)
-def test_shard_consistency_bitwise(kernel):
+def test_shard_consistency_bitwise():
     """A (b, h) shard computed on its own equals the same slices of the full
     run bit for bit: the multi-GPU split by (b, h) changes no result."""
     q, k, v = seeded_qkv(4, 8, 1024, 128, torch.bfloat16, seed=15)
-    o, m, l = attention_capi(q, k, v, True, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, True)
     qs, ks, vs = (t.reshape(32, 1, 1024, 128)[5:13].contiguous() for t in (q, k, v))
-    o2, m2, l2 = attention_capi(qs, ks, vs, True, kernel=kernel)
+    o2, m2, l2 = attention_capi(qs, ks, vs, True)
     assert torch.equal(o.reshape(32, 1, 1024, 128)[5:13], o2)
     assert torch.equal(m.reshape(32, 1, 1024)[5:13], m2)
     assert torch.equal(l.reshape(32, 1, 1024)[5:13], l2)
 
 
-@pytest.mark.parametrize("kernel", [0] + TCK)
-def test_deterministic_repeat(kernel):
+def test_deterministic_repeat():
     q, k, v = seeded_qkv(2, 4, 2048, 128, torch.bfloat16, seed=16)
-    a = attention_capi(q, k, v, True, kernel=kernel)
-    b = attention_capi(q, k, v, True, kernel=kernel)
+    a = attention_capi(q, k, v, True)
+    b = attention_capi(q, k, v, True)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
 
 
-@pytest.mark.parametrize("kernel", [0] + TCK)
-def test_causality_future_keys_do_not_leak(kernel):
+def test_causality_future_keys_do_not_leak():
     """Changing keys/values after row r leaves rows <= r bit-identical."""
     q, k, v = seeded_qkv(1, 4, 1000, 64, torch.bfloat16, seed=17)
-    o, m, l = attention_capi(q, k, v, True, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, True)
     k2, v2 = k.clone(), v.clone()
     k2[:, :, 600:] = torch.randn_like(k2[:, :, 600:].float()).to(k2.dtype) * 3
     v2[:, :, 600:] = 7.0
-    o2, m2, l2 = attention_capi(q, k2, v2, True, kernel=kernel)
+    o2, m2, l2 = attention_capi(q, k2, v2, True)
     assert torch.equal(o[:, :, :600], o2[:, :, :600])
     assert torch.equal(m[:, :, :600], m2[:, :, :600])
     assert not torch.equal(o[:, :, 600:], o2[:, :, 600:])
 
 
-@pytest.mark.parametrize("kernel", [0] + TCK)
-def test_output_bounds_full_size(kernel):
+def test_output_bounds_full_size():
     """At config-3 size: every O row is a convex combination of V rows, so each
     element lies within the column range of V; 1 <= l <= number of keys."""
     q, k, v = seeded_qkv(16, 32, 4096, 128, torch.bfloat16, seed=18)
-    o, m, l = attention_capi(q, k, v, True, kernel=kernel)
+    o, m, l = attention_capi(q, k, v, True)
     vd = v.cuda().float()
     vmin = vd.amin(dim=2, keepdim=True)
     vmax = vd.amax(dim=2, keepdim=True)
@@ -308,10 +292,9 @@ def test_output_bounds_full_size(kernel):
     assert bool(torch.isfinite(m.float()).all())
 
 
-@pytest.mark.parametrize("kernel", TCK)
-def test_simt_and_tc_agree(kernel):
+def test_simt_and_tc_agree():
     q, k, v = seeded_qkv(2, 4, 700, 128, torch.bfloat16, seed=19)
-    a = attention_capi(q, k, v, True, out_fp32=True, kernel=kernel)
+    a = attention_capi(q, k, v, True, out_fp32=True, kernel=TC)
     b = attention_capi(q, k, v, True, out_fp32=True, kernel=SIMT)
     # each is within 2e-3 of the oracle, so they are within 4e-3 of each other
     assert (a[0] - b[0]).abs().max().item() < 4e-3

@@ -15,7 +15,6 @@ from pmkl_function import fused_self_attention
 pytestmark = pytest.mark.gpu
 
 TC = pmkl_b200.KERNEL_TCGEN05
-DB = pmkl_b200.KERNEL_TCGEN05_DB
 SIMT = pmkl_b200.KERNEL_SIMT
 
 
@@ -51,7 +50,6 @@ def bshd_view(B, H, S, D, dtype, seed):
 
 
 @pytest.mark.parametrize("kernel,dtype,D", [(TC, torch.bfloat16, 128), (TC, torch.float16, 64),
-                                            (DB, torch.bfloat16, 128), (DB, torch.float16, 64),
                                             (SIMT, torch.float32, 64), (SIMT, torch.bfloat16, 96)])
 @pytest.mark.parametrize("causal", [True, False])
 def test_bshd_views_match_contiguous(kernel, dtype, D, causal):
@@ -64,7 +62,7 @@ def test_bshd_views_match_contiguous(kernel, dtype, D, causal):
         assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("kernel", [TC, DB, SIMT])
+@pytest.mark.parametrize("kernel", [TC, SIMT])
 def test_strided_output(kernel):
     B, H, S, D = 2, 3, 257, 128
     q, k, v = (randn((B, H, S, D), torch.bfloat16, s) for s in (4, 5, 6))
@@ -74,7 +72,7 @@ def test_strided_output(kernel):
     assert torch.equal(o_bshd.transpose(1, 2), ref[0]) and torch.equal(m, ref[1]) and torch.equal(l, ref[2])
 
 
-@pytest.mark.parametrize("kernel", [TC, DB, SIMT])
+@pytest.mark.parametrize("kernel", [TC, SIMT])
 def test_strided_fp32_output(kernel):
     B, H, S, D = 1, 2, 200, 64
     q, k, v = (bshd_view(B, H, S, D, torch.float16, s) for s in (7, 8, 9))
@@ -84,7 +82,7 @@ def test_strided_fp32_output(kernel):
     assert torch.equal(o_bshd.transpose(1, 2), ref[0]) and torch.equal(m, ref[1])
 
 
-@pytest.mark.parametrize("kernel", [TC, DB, SIMT])
+@pytest.mark.parametrize("kernel", [TC, SIMT])
 @pytest.mark.parametrize("kv_heads", [1, 2, 4])
 @pytest.mark.parametrize("D", [64, 128])
 def test_grouped_query_matches_repeated_kv(kv_heads, D, kernel):
