@@ -259,6 +259,12 @@ int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, voi
     const long long kv_bytes = 2LL * S * D * 2;
     long long grp = PMKL_PP_GROUP_BYTES / (kv_bytes > 0 ? kv_bytes : 1);
     if (grp < 1) grp = 1;
+    // Small problems (all slices' K and V within about one and a half L2s, as a
+    // GPU's shard of config 3 on 8 GPUs): one longest-first list over every
+    // slice balances the SMs better than L2-sized groups, whose repeated
+    // long-to-short runs leave SMs idle at the end (B200, 64 slices of config
+    // 3: 851 vs 779 TFLOP/s; at 128 slices the groups still win, 875 vs 827).
+    if (kv_bytes * BH <= 8LL * PMKL_PP_GROUP_BYTES) grp = BH;
     if (grp > BH) grp = BH;
     p.group = static_cast<int>(grp);
     p.causal = causal;
