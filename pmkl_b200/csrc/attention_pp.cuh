@@ -53,6 +53,12 @@ __host__ __device__ constexpr uint32_t col_o(int x) { return x ? 384u : 256u; } 
 // scores 64-127 stay intact in tensor memory until the next S.
 constexpr uint32_t kPHi = 0;   // P (hi) columns inside an S buffer
 constexpr uint32_t kPLo = 64;  // P (lo) columns inside an S buffer
+// Head size 64: O takes 64 columns, which leaves room for a P buffer of its
+// own per query tile (P_A [320,384), P_B [448,512)).  P then never aliases S,
+// so a tile's next S is issued as soon as the softmax has read S, without
+// waiting for P.V: the softmax packs P in registers, signals "S read", waits
+// for the previous P.V to have read the P buffer and stores P.
+__host__ __device__ constexpr uint32_t col_p64(int x) { return x ? 448u : 320u; }
 
 // Register budget per warpgroup after the split (launch: 512 x 128 = 65536).
 // The softmax warpgroups hold a 128-score row each; 184 keeps their loop
@@ -80,7 +86,7 @@ struct Cfg {
     static constexpr int kOffRing = kOffStage + kBoxBytes;
     static constexpr int kOffStats = kOffRing + kStages * kTile;  // [2][128] x {m_used, m_true, l}
     static constexpr int kOffBars = kOffStats + 2 * 128 * 3 * 4;
-    static constexpr int kNumBars = 4 + 2 * kStages + 2 + 2 + 2 + 2 + 2 + 2 + 3;
+    static constexpr int kNumBars = 4 + 2 * kStages + 2 + 2 + 2 + 2 + 2 + 2 + 3 + 4;
     static constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
     static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -182,8 +188,11 @@ __device__ __forceinline__ float2 exp2_poly(float2 x) {
 // tiles whose rows see at most 128 keys) and the plain form from one place
 // each, so that only one copy of the hot loop competes for the instruction
 // cache with the MMA-issuing warp.
-template <bool BF16, bool HILO, int NPOLY>
-__device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2, float mref, uint32_t sa, bool poly) {
+// DEFER: P (hi) goes to `pbuf` (32-bit words, two keys each) instead of
+// tensor memory; the caller stores it later.
+template <bool BF16, bool HILO, int NPOLY, bool DEFER = false>
+__device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2, float mref, uint32_t sa, bool poly,
+                                                uint32_t (&pbuf)[64]) {
     using namespace ptx;
     float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     const float2 c22 = make_float2(c2, c2);
@@ -205,7 +214,12 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2,
                 pl[i] = pack2<BF16>(e.x - h0, e.y - h1);
             }
         }
-        tmem_st16(sa + kPHi + c0 / 2, ph);
+        if constexpr (DEFER) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pbuf[c0 / 2 + i] = ph[i];
+        } else {
+            tmem_st16(sa + kPHi + c0 / 2, ph);
+        }
         if constexpr (HILO) tmem_st16(sa + kPLo + c0 / 2, pl);
     }
     const float2 rr = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
@@ -217,9 +231,9 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float c2,
 // above, and (TRACK) the row maximum of these scores gathered on the side in
 // four running maxima, so that the maximum is off the path from S to P.
 // Returns the partial row sum as a pair.
-template <bool BF16, int NPOLY, int C0, int C1, bool TRACK>
+template <bool BF16, int NPOLY, int C0, int C1, bool TRACK, bool DEFER = false>
 __device__ __forceinline__ float2 exp_chunks(const float (&s)[128], float2 c22, float2 nm2, uint32_t sa, bool poly,
-                                             float (&mx)[4]) {
+                                             float (&mx)[4], uint32_t (&pbuf)[64]) {
     using namespace ptx;
     float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -234,7 +248,12 @@ __device__ __forceinline__ float2 exp_chunks(const float (&s)[128], float2 c22, 
             rs2[i & 1] = add2(rs2[i & 1], e);
             ph[i] = pack2<BF16>(e.x, e.y);
         }
-        tmem_st16(sa + kPHi + c0 / 2, ph);
+        if constexpr (DEFER) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pbuf[c0 / 2 + i] = ph[i];
+        } else {
+            tmem_st16(sa + kPHi + c0 / 2, ph);
+        }
     }
     return add2(rs2[0], rs2[1]);
 }
@@ -277,7 +296,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *mma_done = st_empty + 2;
     uint64_t *stg_written = mma_done + 1;  // epilogue warps -> store thread
     uint64_t *stg_free = stg_written + 1;  // store thread -> epilogue warps
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(stg_free + 1);
+    uint64_t *s_read = stg_free + 1;       // [2] head size 64: the softmax has read S_X
+    uint64_t *pv_done = s_read + 2;        // [2] head size 64: P.V of tile X complete
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pv_done + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -294,6 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&o_empty[x], 4);
             mbar_init(&st_full[x], 4);
             mbar_init(&st_empty[x], 4);
+            mbar_init(&s_read[x], 4);
+            mbar_init(&pv_done[x], 1);
         }
         for (int s = 0; s < NS; ++s) {
             mbar_init(&kv_full[s], 1);
@@ -344,16 +367,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 };
                 if (w.act[0]) load_q(0, qc0);
                 if (w.act[1]) load_q(1, qc1);
-                for (int j = 0; ok && j < w.n_max; ++j) {
-                    for (int kv = 0; kv < 2; ++kv) {
-                        const int s = kvc % NS;
-                        if (kvc >= NS && !(ok = mbar_wait(&kv_empty[s], ((kvc / NS) - 1) & 1, abort_flag))) break;
-                        mbar_arrive_expect_tx(&kv_full[s], TILE);
-                        const CUtensorMap *map = kv ? &tm_v : &tm_k;
-                        for (int b = 0; b < C::kBoxes; ++b)
-                            tma_load_4d(sRing + s * TILE + b * kBoxBytes, map, &kv_full[s], b * kBoxCols, j * 128, hkv,
-                                        bb);
-                        ++kvc;
+                // One K or V tile into the next ring stage.
+                auto load_kv = [&](const int kv, const int jt) {
+                    if (!ok) return;
+                    const int s = kvc % NS;
+                    if (kvc >= NS && !(ok = mbar_wait(&kv_empty[s], ((kvc / NS) - 1) & 1, abort_flag))) return;
+                    mbar_arrive_expect_tx(&kv_full[s], TILE);
+                    const CUtensorMap *map = kv ? &tm_v : &tm_k;
+                    for (int b = 0; b < C::kBoxes; ++b)
+                        tma_load_4d(sRing + s * TILE + b * kBoxBytes, map, &kv_full[s], b * kBoxCols, jt * 128, hkv, bb);
+                    ++kvc;
+                };
+                if constexpr (D == 64) {
+                    // The issuer's order here: K0, then K(j+1) and V(j) per key tile.
+                    load_kv(0, 0);
+                    for (int j = 0; ok && j < w.n_max; ++j) {
+                        if (j + 1 < w.n_max) load_kv(0, j + 1);
+                        load_kv(1, j);
+                    }
+                } else {
+                    for (int j = 0; ok && j < w.n_max; ++j) {
+                        load_kv(0, j);
+                        load_kv(1, j);
                     }
                 }
             }
@@ -368,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ------------------------------------------------------------ MMA issuer
             constexpr uint32_t kIdescS = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
             constexpr uint32_t kIdescO = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
-            uint32_t qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0, oc0 = 0, oc1 = 0;
+            uint32_t qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0, oc0 = 0, oc1 = 0, rc0 = 0, rc1 = 0;
             int kvc = 0;
             bool ok = true;
             // Descriptors are built once; every operand slice is then the base
@@ -396,9 +431,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t b0 = v_lo + static_cast<uint32_t>(stage * (TILE >> 4));
                 const uint32_t d = tmem + col_o(x);
                 const uint32_t a = tmem + col_s(x);
+                const uint32_t ahi = (D == 64) ? tmem + col_p64(x) : a + kPHi;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_ts_h(d, a + kPHi + kk * 8, b0 + static_cast<uint32_t>(kk * 128), v_hi, kIdescO,
+                    mma_ts_h(d, ahi + kk * 8, b0 + static_cast<uint32_t>(kk * 128), v_hi, kIdescO,
                              (!first || kk > 0) ? 1u : 0u);
                 if (hilo) {
 #pragma unroll
@@ -433,6 +469,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (n1 == 1) mma_commit(&q_empty[1]);
                 }
                 mma_commit(&kv_empty[sK]);
+                if constexpr (D == 64) {
+                    // Per key tile j and query tile X: S_X(j+1) once the softmax has
+                    // read S_X(j), then P.V_X(j) once P_X(j) is stored.
+                    for (int j = 0; ok && j < w.n_max; ++j) {
+                        const bool has_next = j + 1 < w.n_max;
+                        if (has_next) {
+                            sK = kvc % NS;
+                            if (!(ok = mbar_wait(&kv_full[sK], (kvc / NS) & 1, abort_flag))) break;
+                            ++kvc;
+                        }
+                        const int sV = kvc % NS;
+                        if (!(ok = mbar_wait(&kv_full[sV], (kvc / NS) & 1, abort_flag))) break;
+                        ++kvc;
+                        auto tile64 = [&](const int x, const int nx, const bool hlx, uint32_t &rcx, uint32_t &pcx,
+                                          uint32_t &ocx) {
+                            if (!ok || j >= nx) return;
+                            if (!(ok = mbar_wait(&s_read[x], rcx & 1, abort_flag))) return;
+                            ++rcx;
+                            if (j + 1 < nx) {
+                                tc_fence_after();
+                                issue_s(x, sK);
+                                if (j + 2 == nx) mma_commit(&q_empty[x]);
+                            }
+                            if (!(ok = mbar_wait(&p_full[x], pcx & 1, abort_flag))) return;
+                            ++pcx;
+                            if (j == 0 && ocx > 0 && !(ok = mbar_wait(&o_empty[x], (ocx - 1) & 1, abort_flag)))
+                                return;
+                            tc_fence_after();
+                            issue_pv(x, sV, j == 0, hlx);
+                            mma_commit(&pv_done[x]);
+                            if (j + 1 == nx) {
+                                mma_commit(&o_full[x]);
+                                ++ocx;
+                            }
+                        };
+                        tile64(0, n0, hl0, rc0, pc0, oc0);
+                        tile64(1, n1, hl1, rc1, pc1, oc1);
+                        if (!ok) break;
+                        if (has_next) mma_commit(&kv_empty[sK]);
+                        mma_commit(&kv_empty[sV]);
+                    }
+                    continue;
+                }
                 for (int j = 0; ok && j < w.n_max; ++j) {
                     const int sV = kvc % NS;
                     if (!(ok = mbar_wait(&kv_full[sV], (kvc / NS) & 1, abort_flag))) break;
@@ -486,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t sa = lane_base + col_s(x);
             const float c2 = p.scale_log2;
             int sc = 0, uc = 0;
+            uint32_t pvc = 0;  // head size 64: P tiles stored so far (one P.V each)
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
                 const Unit w = decode(p, u);
@@ -502,6 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (p.causal) lim = min(lim, row - kbase + 1);
                     const bool masked = __any_sync(0xffffffffu, lim < 128);
                     float s[128];
+                    uint32_t pbuf[64];  // head size 64: P (hi) until the P buffer is free
                     uint32_t *sr = reinterpret_cast<uint32_t *>(s);
                     auto mask_half = [&](const int h) {
                         if (masked) {
@@ -543,9 +624,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         m_new = m_true;
                         const float mref = (m_new == -INFINITY) ? 0.f : m_new * c2;
                         if (hilox)
-                            rsum = exp_pack_store<BF16, true, 0>(s, c2, mref, sa, false);
+                            rsum = exp_pack_store<BF16, true, 0, D == 64>(s, c2, mref, sa, false, pbuf);
                         else
-                            rsum = exp_pack_store<BF16, false, NPOLY>(s, c2, mref, sa, !masked);
+                            rsum = exp_pack_store<BF16, false, NPOLY, D == 64>(s, c2, mref, sa, !masked, pbuf);
                         fac = 0.f;  // l and O hold nothing yet
                         any_fac = false;
                     } else {
@@ -569,10 +650,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
                         mask_half(0);
                         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-                        float2 r = exp_chunks<BF16, NPOLY, 0, 64, true>(s, c22, nm2, sa, !masked, mx);
+                        float2 r = exp_chunks<BF16, NPOLY, 0, 64, true, D == 64>(s, c22, nm2, sa, !masked, mx, pbuf);
                         tmem_wait_ld();
                         mask_half(1);
-                        r = add2(r, exp_chunks<BF16, NPOLY, 64, 128, true>(s, c22, nm2, sa, !masked, mx));
+                        r = add2(r, exp_chunks<BF16, NPOLY, 64, 128, true, D == 64>(s, c22, nm2, sa, !masked, mx, pbuf));
                         m_true = fmaxf(m_true, fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]));
                         constexpr float kSpec = BF16 ? 30.0f : 15.0f;
                         const bool redo = (m_true - m_new) * c2 > kSpec;
@@ -580,22 +661,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // Rare: scores 64-127 are reloaded (P went to the
                             // columns of scores 0-63), scores 0-63 are still in
                             // registers.
+                            if constexpr (D == 64) {
+                                // S is untouched by P here: reload every score.
+                                tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                                tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                            }
                             tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
                             tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
                             tmem_wait_ld();
+                            if constexpr (D == 64) mask_half(0);
                             mask_half(1);
                             if (redo) m_new = m_true;
                             nm2 = make_float2(-m_new * c2, -m_new * c2);
                             tmem_wait_st();
                             float unused[4];
-                            r = exp_chunks<BF16, 0, 0, 128, false>(s, c22, nm2, sa, false, unused);
+                            r = exp_chunks<BF16, 0, 0, 128, false, D == 64>(s, c22, nm2, sa, false, unused, pbuf);
                         }
                         rsum = r.x + r.y;
                         fac = (m_new == m_used) ? 1.f : ex2_approx((m_used - m_new) * c2);
                         any_fac = __any_sync(0xffffffffu, m_new != m_used);
                     }
-                    // O_X is idle here: S_X(j) was issued after PV_X(j-1), and
-                    // its commit covers every earlier MMA.
+                    if constexpr (D == 64) {
+                        // S_X may be overwritten from here on; P goes to its own
+                        // buffer once P.V of the previous key tile has read it
+                        // (which also leaves O_X idle for the rescale below).
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&s_read[x]);
+                        if (pvc > 0 && !(ok = mbar_wait_warp(&pv_done[x], (pvc - 1) & 1, abort_flag))) break;
+                        ++pvc;
+                        tc_fence_after();
+                        tmem_st32(lane_base + col_p64(x), *reinterpret_cast<uint32_t(*)[32]>(pbuf));
+                        tmem_st32(lane_base + col_p64(x) + 32, *reinterpret_cast<uint32_t(*)[32]>(pbuf + 32));
+                    }
+                    // O_X is idle here (head size 128: S_X(j) was issued after PV_X(j-1),
+                    // and its commit covers every earlier MMA).
                     if (any_fac) {
 #pragma unroll
                         for (int cc = 0; cc < D / 32; ++cc) {
