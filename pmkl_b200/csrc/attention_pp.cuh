@@ -510,44 +510,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (has_next) mma_commit(&kv_empty[sK]);
                         mma_commit(&kv_empty[sV]);
                     }
-                    continue;
-                }
-                for (int j = 0; ok && j < w.n_max; ++j) {
-                    const int sV = kvc % NS;
-                    if (!(ok = mbar_wait(&kv_full[sV], (kvc / NS) & 1, abort_flag))) break;
-                    ++kvc;
-                    const bool has_next = j + 1 < w.n_max;
-                    const int kvc_next = kvc;
-                    if (has_next) {
-                        sK = kvc % NS;
+                } else {
+                    for (int j = 0; ok && j < w.n_max; ++j) {
+                        const int sV = kvc % NS;
+                        if (!(ok = mbar_wait(&kv_full[sV], (kvc / NS) & 1, abort_flag))) break;
                         ++kvc;
-                    }
-                    bool k_ready = false;
-                    auto tile = [&](const int x, const int nx, const bool hlx, uint32_t &pcx, uint32_t &ocx) {
-                        if (!ok || j >= nx) return;
-                        if (!(ok = mbar_wait(&p_full[x], pcx & 1, abort_flag))) return;
-                        ++pcx;
-                        if (j == 0 && ocx > 0 && !(ok = mbar_wait(&o_empty[x], (ocx - 1) & 1, abort_flag))) return;
-                        tc_fence_after();
-                        issue_pv(x, sV, j == 0, hlx);
-                        if (j + 1 < nx) {
-                            if (!k_ready) {
-                                if (!(ok = mbar_wait(&kv_full[sK], (kvc_next / NS) & 1, abort_flag))) return;
-                                k_ready = true;
-                                tc_fence_after();
-                            }
-                            issue_s(x, sK);
-                            if (j + 2 == nx) mma_commit(&q_empty[x]);
-                        } else {
-                            mma_commit(&o_full[x]);
-                            ++ocx;
+                        const bool has_next = j + 1 < w.n_max;
+                        const int kvc_next = kvc;
+                        if (has_next) {
+                            sK = kvc % NS;
+                            ++kvc;
                         }
-                    };
-                    tile(0, n0, hl0, pc0, oc0);
-                    tile(1, n1, hl1, pc1, oc1);
-                    if (!ok) break;
-                    mma_commit(&kv_empty[sV]);
-                    if (has_next) mma_commit(&kv_empty[sK]);
+                        bool k_ready = false;
+                        auto tile = [&](const int x, const int nx, const bool hlx, uint32_t &pcx, uint32_t &ocx) {
+                            if (!ok || j >= nx) return;
+                            if (!(ok = mbar_wait(&p_full[x], pcx & 1, abort_flag))) return;
+                            ++pcx;
+                            if (j == 0 && ocx > 0 && !(ok = mbar_wait(&o_empty[x], (ocx - 1) & 1, abort_flag))) return;
+                            tc_fence_after();
+                            issue_pv(x, sV, j == 0, hlx);
+                            if (j + 1 < nx) {
+                                if (!k_ready) {
+                                    if (!(ok = mbar_wait(&kv_full[sK], (kvc_next / NS) & 1, abort_flag))) return;
+                                    k_ready = true;
+                                    tc_fence_after();
+                                }
+                                issue_s(x, sK);
+                                if (j + 2 == nx) mma_commit(&q_empty[x]);
+                            } else {
+                                mma_commit(&o_full[x]);
+                                ++ocx;
+                            }
+                        };
+                        tile(0, n0, hl0, pc0, oc0);
+                        tile(1, n1, hl1, pc1, oc1);
+                        if (!ok) break;
+                        mma_commit(&kv_empty[sV]);
+                        if (has_next) mma_commit(&kv_empty[sK]);
+                    }
                 }
             }
             // Drain every MMA issued before tensor memory is released.
