@@ -17,9 +17,17 @@ One JSON line on rank 0:
             timed region; the step's slices go in --e2e-chunks chunks whose
             copies overlap the attention of the neighbouring chunks;
   roofline  the attention kernel's achieved TFLOP/s per launch vs the measured
-            bf16 peak (MEASURED_PEAKS.json);
+            bf16 peak (MEASURED_PEAKS.json), with the exp unit's (MUFU)
+            fraction beside it;
+  clocks    SM clock and clock-event reasons sampled through NVML every few
+            milliseconds during the timed region;
   cpu_baseline  the reference's own CPU implementation (its torch extension
-            compiled from its sources into oracle/_ref) on a bounded sample.
+            compiled from its sources into oracle/_ref) on a bounded sample;
+  sub       the default run also measures BASELINE configs 2 and 4 (attention)
+            and 5 (softmax) the same way, each with its own value, roofline
+            (config 2 against the exp unit, which binds at head size 64;
+            softmax against the measured copy bandwidth), end-to-end leg, CPU
+            baseline and clocks (--no-sub skips them).
 
 --impl reference runs that reference CPU implementation instead, with one
 worker process per host core, each step a bounded sample of the workload.
@@ -66,6 +74,8 @@ def parse_args():
                     help="slice chunks per end-to-end step (copies of one chunk overlap the attention of another)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="default workload only: skip the configs 2, 4 and 5 sub-records")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--kernel", type=int, default=0,
                     help="pmkl_attention_kernel value for the device-timed leg (0 = automatic choice)")
@@ -112,55 +122,73 @@ def profile_traffic(workload: str):
 
 
 # ----------------------------------------------------------------------------- clocks
-class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASON_BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, n_gpus: int, enabled: bool):
-        self.proc = None
-        self.path = None
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons of this rank's GPU
+    every few milliseconds through NVML (read-only queries) on a background
+    thread, so that even a timed region of a few tens of milliseconds holds
+    several samples.  window(t0, t1) summarises the samples taken inside a
+    host-time window.  Falls back to nothing when NVML is unavailable."""
+
+    def __init__(self, local: int, enabled: bool, period_s: float = 0.004):
+        import threading
+
+        self.samples = []
+        self.thread = None
+        self.max_mhz = None
         if not enabled:
             return
-        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        idx = vis if vis else ",".join(str(i) for i in range(n_gpus))
-        out_dir = REPO / "gpurun_out"
-        out_dir.mkdir(exist_ok=True)
-        self.path = out_dir / f"clocks_{os.getpid()}.csv"
         try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", idx, "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+            import torch
 
-    def stop(self) -> dict | None:
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.fh.close()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
+            pynvml.nvmlInit()
+            self.nvml = pynvml
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
+                uuid = str(torch.cuda.get_device_properties(local).uuid)
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[local]) if vis else local
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return
+        self.stop_flag = threading.Event()
+        self.period = period_s
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def _run(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((time.perf_counter(), nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                                     int(get_reasons(self.h)), nv.nvmlDeviceGetPowerUsage(self.h) / 1e3))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def window(self, t0: float, t1: float) -> dict | None:
+        sel = [x for x in list(self.samples) if t0 <= x[0] <= t1]
+        if not sel:
+            # the region was shorter than one sampling period: the nearest sample
+            later = [x for x in list(self.samples) if x[0] >= t0]
+            sel = later[:1]
+        if not sel:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = sorted({n for n, bit in REASON_BITS.items() for x in sel if x[2] & bit})
+        return {"sm_mhz": statistics.median(x[1] for x in sel), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sel), "power_w_max": max(x[3] for x in sel), "source": "NVML, every ~4 ms"}
+
+    def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
 
 
 # ----------------------------------------------------------------------------- dist
@@ -210,14 +238,16 @@ def sum_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def timed_loop(step, steps: int, warmup: int, world: int):
+def timed_loop(step, steps: int, warmup: int, world: int, sampler: "ClockSampler | None" = None):
     """W untimed steps, then K steps between barrier + synchronize; returns
-    (total ms of the K steps, list of per-step ms) on this rank."""
+    (total ms of the K steps, list of per-step ms, clock summary of the timed
+    region or None) on this rank."""
     import torch
 
     for _ in range(warmup):
         step()
     barrier(world)
+    t_host0 = time.perf_counter()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
@@ -228,8 +258,10 @@ def timed_loop(step, steps: int, warmup: int, world: int):
         ev[i][1].record()
     end.record()
     torch.cuda.synchronize()
+    t_host1 = time.perf_counter()
     barrier(world)
-    return start.elapsed_time(end), [a.elapsed_time(b) for a, b in ev]
+    clocks = sampler.window(t_host0, t_host1) if sampler is not None else None
+    return start.elapsed_time(end), [a.elapsed_time(b) for a, b in ev], clocks
 
 
 # ----------------------------------------------------------------------------- reference CPU code
@@ -278,7 +310,11 @@ def pick_bwd_rows(D: int, dtype_name: str, causal: bool, budget_s: float) -> int
 
 
 def _ref_softmax_worker(args):
-    rows, el, seed = args
+    """The reference's host_softmax_forward (compiled from its sources into
+    oracle/_ref) on `rows` seeded rows, `reps` times over the same input;
+    returns the seconds of the calls."""
+    rows, el, seed = args[:3]
+    reps = args[3] if len(args) > 3 else 1
     import numpy as np
 
     from oracle import build_ref
@@ -287,7 +323,8 @@ def _ref_softmax_worker(args):
     x = (np.random.default_rng(seed).standard_normal(rows * el) * 2).astype(np.float32)
     y = np.empty_like(x)
     t0 = time.perf_counter()
-    fn(y.ctypes.data, x.ctypes.data, el, el, rows)
+    for _ in range(reps):
+        fn(y.ctypes.data, x.ctypes.data, el, el, rows)
     return time.perf_counter() - t0
 
 
@@ -318,41 +355,39 @@ def cpu_baseline_attention(S, D, dtype_name, std, causal, budget_s=20.0) -> dict
                       f"of {r} of {S} rows, D={D}, {t:.1f} s on 1 core"}
 
 
-def run_reference_arm(args, wl, rank, world):
-    """--impl reference: the reference's own CPU implementation on all host
-    cores (one process per core), each step a bounded sample."""
+def reference_record(name: str, wl, steps: int, warmup: int, budget_total_s: float) -> dict:
+    """The reference's own CPU implementation of workload `name` on all host
+    cores (one spawn-started process per core), each step a bounded sample."""
     import multiprocessing as mp
 
-    if rank != 0:
-        return None
     B, H, S, D, dtype_name, std, causal, desc = wl
     cores = host_cores()
     ctx = mp.get_context("spawn")
-    total_steps = args.steps + args.warmup
-    budget = max(0.5, min(20.0, 150.0 / max(1, total_steps)))
-    if args.workload == "softmax":
+    total_steps = steps + warmup
+    budget = max(0.5, min(20.0, budget_total_s / max(1, total_steps)))
+    if name == "softmax":
         rows_total, el = B, H
         probe = _ref_softmax_worker((256, el, 0))
         rows = max(1, min(rows_total // cores if rows_total >= cores else rows_total, int(budget / (probe / 256))))
         work = [(rows, el, 100 + i) for i in range(cores)]
         unit_per_step = cores * rows * el * 8.0 / 1e9  # GB moved per step (read + write fp32)
-        unit, metric = "GB/s", "warp softmax GB/s (whole box)"
+        unit, metric = "GB/s", SOFTMAX_METRIC
         sample = f"reference host_softmax_forward (CPU fp32), {rows} rows x {el} per core per step"
-    elif args.workload != "attention-bwd":
-        r = pick_prefix_rows(S, D, dtype_name, causal, budget)
-        work = [(r, D, dtype_name, std, causal, 100 + i) for i in range(cores)]
-        unit_per_step = cores * attn_flops_per_slice(r, D, causal) / 1e12
-        unit, metric = "TFLOP/s", ATTN_METRIC
-        sample = (f"reference fused_self_attention_fw (CPU, {dtype_name}): per step each of {cores} worker "
-                  f"processes runs a causal prefix of {r} of {S} rows of one (b,h) slice, D={D}")
-    elif args.workload == "attention-bwd":
+    elif name == "attention-bwd":
         r = pick_bwd_rows(D, dtype_name, causal, budget)
         work = [(r, D, dtype_name, std, causal, 100 + i) for i in range(cores)]
         unit_per_step = cores * attn_bwd_flops_per_slice(r, D, causal) / 1e12
         unit, metric = "TFLOP/s", BWD_METRIC
         sample = (f"reference fused_self_attention_bw (CPU, {dtype_name}, O(S^3 D)): per step each of {cores} "
                   f"worker processes runs the backward of one {r}-row causal (b,h) problem, D={D}")
-    fn = {"softmax": _ref_softmax_worker, "attention-bwd": _ref_attention_bwd_worker}.get(args.workload,
+    else:
+        r = pick_prefix_rows(S, D, dtype_name, causal, budget)
+        work = [(r, D, dtype_name, std, causal, 100 + i) for i in range(cores)]
+        unit_per_step = cores * attn_flops_per_slice(r, D, causal) / 1e12
+        unit, metric = "TFLOP/s", ATTN_METRIC
+        sample = (f"reference fused_self_attention_fw (CPU, {dtype_name}): per step each of {cores} worker "
+                  f"processes runs a causal prefix of {r} of {S} rows of one (b,h) slice, D={D}")
+    fn = {"softmax": _ref_softmax_worker, "attention-bwd": _ref_attention_bwd_worker}.get(name,
                                                                                           _ref_attention_worker)
     times = []
     with ctx.Pool(cores) as pool:
@@ -360,24 +395,70 @@ def run_reference_arm(args, wl, rank, world):
             t0 = time.perf_counter()
             pool.map(fn, work, chunksize=1)
             dt = time.perf_counter() - t0
-            if i >= args.warmup:
+            if i >= warmup:
                 times.append(dt)
     tot = sum(times)
     value = unit_per_step * len(times) / tot
-    line = {
-        "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
+    return {
+        "impl": "reference", "metric": metric, "value": value, "unit": unit,
+        "steps": steps, "warmup": warmup, "ms_per_step": 1e3 * tot / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name,
         "data": "synthetic (seeded N(0, std^2))",
         "config": {"workload": desc, "sample": sample},
         "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def run_reference_arm(args, wl, rank, world):
+    """--impl reference: the main workload, then (default run) the same
+    sub-workloads as the B200 arm with a few steps each."""
+    if rank != 0:
+        return None
+    line = reference_record(args.workload, wl, args.steps, args.warmup, 150.0)
+    line["n_gpus"] = args.gpus
+    if sub_records_enabled(args):
+        line["sub"] = {}
+        for key, name, _, _, _ in SUB_RECORDS:
+            rec = reference_record(name, WORKLOADS[name], min(args.steps, 4), 1, 20.0)
+            line["sub"][key] = rec
     return line
 
 
 # ----------------------------------------------------------------------------- B200 arm
-def run_attention(args, wl, rank, world, local):
+# Sub-records the default run adds to its line: (key, workload, minimum timed
+# steps, end-to-end steps, single-core CPU baseline budget in seconds).
+SUB_RECORDS = [
+    ("attention_cfg2", "attention-cfg2", 200, 5, 10.0),
+    ("attention_cfg4", "attention-cfg4", 20, 3, 10.0),
+    ("softmax_cfg5", "softmax", 100, 5, None),
+]
+SOFTMAX_METRIC = "warp softmax GB/s (whole box)"
+MUFU_EX2_PER_CLK_PER_SM = 16  # nominal sm_100 exp2 (MUFU) throughput
+
+
+def sub_records_enabled(args) -> bool:
+    return args.workload == "attention" and not args.shape and not args.no_sub
+
+
+def sm_count(local: int) -> int:
+    import torch
+
+    return torch.cuda.get_device_properties(local).multi_processor_count
+
+
+def mufu_roofline(exps_per_launch: float, launch_ms: float, clocks: dict | None, n_sm: int) -> dict:
+    """Exp-unit roofline: algorithmic exps (one per unmasked score) per launch
+    over the launch time, against 16 ex2 per clock per SM at the median SM
+    clock sampled during the timed region."""
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    peak = MUFU_EX2_PER_CLK_PER_SM * n_sm * mhz * 1e6 / 1e9
+    achieved = exps_per_launch / (launch_ms / 1e3) / 1e9
+    return {"achieved": achieved, "peak": peak, "unit": "Gexp/s", "frac": achieved / peak,
+            "peak_source": f"nominal {MUFU_EX2_PER_CLK_PER_SM} ex2/clk/SM x {n_sm} SMs at {mhz:.0f} MHz (sampled)"}
+
+
+def run_attention(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget):
     import torch
 
     import pmkl_b200
@@ -401,17 +482,16 @@ def run_attention(args, wl, rank, world, local):
 
     kernel_name = pmkl_b200.attention_kernel_name(q, k, v, o, args.kernel)
 
-    sampler = ClockSampler(world, (not args.no_clocks) and rank == 0)
-    total_ms, per_ms = timed_loop(step, args.steps, args.warmup, world)
-    clocks = sampler.stop()
+    total_ms, per_ms, clocks = timed_loop(step, steps, args.warmup, world, sampler)
     flops_rank = ns * attn_flops_per_slice(S, D, causal)
     flops_all = n_slices * attn_flops_per_slice(S, D, causal)
     t_max = max_over_ranks(total_ms, world)
-    value = flops_all * args.steps / (t_max / 1e3) / 1e12
+    value = flops_all * steps / (t_max / 1e3) / 1e12
     launch_avg = statistics.mean(per_ms)
     achieved = flops_rank / (launch_avg / 1e3) / 1e12
     achieved_min = max_over_ranks(-achieved, world)  # slowest rank
     peaks = measured_peaks()
+    pairs = S * (S + 1) / 2 if causal else S * S
 
     # End to end through the public API: every step copies q, k, v in from
     # pinned host memory, calls fused_self_attention and copies O, m, l back.
@@ -451,54 +531,67 @@ def run_attention(args, wl, rank, world, local):
                 lh[a:b].copy_(ol, non_blocking=True)
         main.wait_stream(s_out)
 
-    e2e_steps = max(1, min(args.e2e_steps, args.steps))
-    e2e_ms, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
+    e2e_steps = max(1, min(e2e_steps, steps))
+    e2e_ms, _, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
     e2e_t = max_over_ranks(e2e_ms, world)
     e2e_value = flops_all * e2e_steps / (e2e_t / 1e3) / 1e12
     h2d = 3 * q.numel() * q.element_size()
     d2h = o.numel() * o.element_size() + 2 * m.numel() * m.element_size()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cpu_budget:
         try:
-            cpu = cpu_baseline_attention(S, D, dtype_name, std, causal)
+            cpu = cpu_baseline_attention(S, D, dtype_name, std, causal, cpu_budget)
         except FileNotFoundError as e:
             cpu = {"value": None, "unit": "TFLOP/s", "cores": 1, "kind": "reference",
                    "sample": f"unavailable: {e}"}
 
-    traffic = profile_traffic(args.workload)
+    traffic = profile_traffic(name)
+    tensor = {"bound": "tensor", "achieved": -achieved_min, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+              "frac": -achieved_min / peaks["bf16_tflops"],
+              "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
+              "traffic": (traffic * ns if traffic is not None else None),
+              "algorithmic_bytes": 4 * q.numel() * q.element_size() + 2 * m.numel() * m.element_size(),
+              "kernel": kernel_name, "launch_ms_avg": launch_avg}
+    mufu = mufu_roofline(ns * pairs, launch_avg, clocks, sm_count(local))
+    if D == 64:
+        # Head size 64: a key tile of a 128-row query tile costs 16384 exps
+        # (1024 MUFU cycles) against 4.2 MFLOP of contractions (512 tensor
+        # cycles), so the exp unit is the binding roofline.
+        roofline = dict(mufu, bound="mufu", kernel=kernel_name, launch_ms_avg=launch_avg,
+                        traffic=tensor["traffic"], algorithmic_bytes=tensor["algorithmic_bytes"],
+                        tensor={k: tensor[k] for k in ("achieved", "peak", "unit", "frac", "peak_source")})
+    else:
+        roofline = dict(tensor, mufu=mufu)
     line = {
-        "metric": ATTN_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "metric": ATTN_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": t_max / steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": dtype_name, "data": f"synthetic, seeded N(0, {std}^2) generated on device",
         "config": {"workload": desc, "B": B, "H": H, "S": S, "D": D, "causal": causal,
                    "parallelism": f"(batch, head) shards over {world} GPU(s), no inter-GPU traffic",
                    "slices_per_gpu": ns, "flop_convention": "4*D*S(S+1)/2 per (b,h) slice",
-                   "l2": "inputs (3 x %.0f MiB per GPU) exceed the 126 MB L2; no flush" % (q.numel() * q.element_size() / 2**20)},
+                   "l2": ("inputs (3 x %.0f MiB per GPU) exceed the 126 MB L2; no flush"
+                          % (q.numel() * q.element_size() / 2**20)) if 3 * q.numel() * q.element_size() > 126e6
+                   else "inputs fit in L2: every timed launch reads them from L2 after the first"},
         "per_gpu_tflops": value / world,
         "frac_of_peak": value / world / peaks["bf16_tflops"],
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "pmkl_function.fused_self_attention", "steps": e2e_steps,
                 "chunks": n_chunks, "overlap": "H2D / attention / D2H of consecutive chunks on three streams"},
-        "gpu_launches": args.steps,
-        "roofline": {"bound": "tensor", "achieved": -achieved_min, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": -achieved_min / peaks["bf16_tflops"],
-                     "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
-                     "traffic": (traffic * ns if traffic is not None else None),
-                     "algorithmic_bytes": 4 * q.numel() * q.element_size() + 2 * m.numel() * m.element_size(),
-                     "kernel": kernel_name, "launch_ms_avg": launch_avg},
+        "gpu_launches": steps,
+        "roofline": roofline,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
     return line
 
 
-def run_attention_bwd(args, wl, rank, world, local):
+def run_attention_bwd(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget):
     """One step = pmkl_causal_attention_bwd over the rank's (b, h) shard: the
-    forward with fp32 outputs (delta needs O, which the reference's backward
-    does not take), the row-statistics kernel, the dQ kernel and the dK/dV
-    kernel.  m, l come from one forward before the timed region, in the input
-    dtype as the reference returns them."""
+    persistent forward in its backward instantiation (per-row b and delta from
+    its epilogue), the dQ kernel and the dK/dV kernel.  m, l come from one
+    forward before the timed region, in the input dtype as the reference
+    returns them."""
     import torch
 
     import pmkl_b200
@@ -517,20 +610,19 @@ def run_attention_bwd(args, wl, rank, world, local):
     l = torch.empty_like(m)
     pmkl_b200.attention_fwd(q, k, v, o, m, l, causal)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    ws = torch.empty(pmkl_b200.attention_bwd_workspace_size(ns, 1, S, D, dt), dtype=torch.uint8, device=dev)
+    ws = torch.empty(pmkl_b200.attention_bwd_workspace_size(ns, 1, S, D, dt, args.kernel), dtype=torch.uint8,
+                     device=dev)
     stream = torch.cuda.current_stream()
 
     def step():
         pmkl_b200.attention_bwd(do, q, k, v, m, l, dq, dk, dv, causal, kernel=args.kernel, workspace=ws,
                                 stream=stream)
 
-    sampler = ClockSampler(world, (not args.no_clocks) and rank == 0)
-    total_ms, per_ms = timed_loop(step, args.steps, args.warmup, world)
-    clocks = sampler.stop()
+    total_ms, per_ms, clocks = timed_loop(step, steps, args.warmup, world, sampler)
     flops_rank = ns * attn_bwd_flops_per_slice(S, D, causal)
     flops_all = n_slices * attn_bwd_flops_per_slice(S, D, causal)
     t_max = max_over_ranks(total_ms, world)
-    value = flops_all * args.steps / (t_max / 1e3) / 1e12
+    value = flops_all * steps / (t_max / 1e3) / 1e12
     launch_avg = statistics.mean(per_ms)
     achieved = -max_over_ranks(-(flops_rank / (launch_avg / 1e3) / 1e12), world)
     peaks = measured_peaks()
@@ -567,16 +659,16 @@ def run_attention_bwd(args, wl, rank, world, local):
                     h_[a:b].copy_(g_, non_blocking=True)
         main.wait_stream(s_out)
 
-    e2e_steps = max(1, min(args.e2e_steps, args.steps))
-    e2e_ms, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
+    e2e_steps = max(1, min(e2e_steps, steps))
+    e2e_ms, _, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
     e2e_value = flops_all * e2e_steps / (max_over_ranks(e2e_ms, world) / 1e3) / 1e12
     h2d = sum(t.numel() * t.element_size() for t in hosts)
     d2h = sum(t.numel() * t.element_size() for t in outs_h)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cpu_budget:
         try:
-            r = pick_bwd_rows(D, dtype_name, causal, 15.0)
+            r = pick_bwd_rows(D, dtype_name, causal, cpu_budget)
             tt = _ref_attention_bwd_worker((r, D, dtype_name, std, causal, 7))
             cpu = {"value": attn_bwd_flops_per_slice(r, D, causal) / tt / 1e12, "unit": "TFLOP/s", "cores": 1,
                    "kind": "reference",
@@ -586,8 +678,8 @@ def run_attention_bwd(args, wl, rank, world, local):
             cpu = {"value": None, "unit": "TFLOP/s", "cores": 1, "kind": "reference", "sample": f"unavailable: {e}"}
 
     return {
-        "metric": BWD_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "metric": BWD_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": t_max / steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": dtype_name, "data": f"synthetic, seeded N(0, {std}^2) generated on device",
         "config": {"workload": desc, "B": B, "H": H, "S": S, "D": D, "causal": causal,
                    "parallelism": f"(batch, head) shards over {world} GPU(s), no inter-GPU traffic",
@@ -598,20 +690,20 @@ def run_attention_bwd(args, wl, rank, world, local):
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "pmkl_pytorch_ext.fused_self_attention_bw", "steps": e2e_steps,
                 "chunks": n_chunks, "overlap": "H2D / backward / D2H of consecutive chunks on three streams"},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": (4 if args.kernel == 3 else 3) * steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"],
                      "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
                      "traffic": None,
-                     "kernel": "one backward call: attn_fwd_pp_kernel (fp32 out) + bwd_rowstat_kernel + "
-                               "attn_bwd_dq_kernel + attn_bwd_dkv_kernel",
+                     "kernel": "one backward call: attn_fwd_pp_kernel (delta epilogue) + attn_bwd_dq_kernel + "
+                               "attn_bwd_dkv_kernel",
                      "launch_ms_avg": launch_avg},
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
 
 
-def run_softmax(args, wl, rank, world, local):
+def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget):
     import torch
 
     import pmkl_b200
@@ -628,13 +720,11 @@ def run_softmax(args, wl, rank, world, local):
     def step():
         pmkl_b200.warp_softmax_fwd(y, x, el, el, rows, stream=stream)
 
-    sampler = ClockSampler(world, (not args.no_clocks) and rank == 0)
-    total_ms, per_ms = timed_loop(step, args.steps, args.warmup, world)
-    clocks = sampler.stop()
+    total_ms, per_ms, clocks = timed_loop(step, steps, args.warmup, world, sampler)
     bytes_rank = 2.0 * rows * el * 4
     bytes_all = 2.0 * rows_all * el * 4
     t_max = max_over_ranks(total_ms, world)
-    value = bytes_all * args.steps / (t_max / 1e3) / 1e9
+    value = bytes_all * steps / (t_max / 1e3) / 1e9
     launch_avg = statistics.mean(per_ms)
     achieved = -max_over_ranks(-(bytes_rank / (launch_avg / 1e3) / 1e9), world)
     peaks = measured_peaks()
@@ -665,30 +755,34 @@ def run_softmax(args, wl, rank, world, local):
                 yh[a:b].copy_(yd[a:b], non_blocking=True)
         main.wait_stream(s_out)
 
-    e2e_steps = max(1, min(args.e2e_steps, args.steps))
-    e2e_ms, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
+    e2e_steps = max(1, min(e2e_steps, steps))
+    e2e_ms, _, _ = timed_loop(e2e_step, e2e_steps, min(args.warmup, 3), world)
     e2e_value = bytes_all * e2e_steps / (max_over_ranks(e2e_ms, world) / 1e3) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            n = 8192
-            t = _ref_softmax_worker((n, el, 9))
-            cpu = {"value": n * el * 8.0 / t / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference",
-                   "sample": f"reference host_softmax_forward (CPU fp32) on {n} rows x {el}, {t:.2f} s on 1 core"}
+            # the whole problem (all rows_all rows), repeated for ~5 s of CPU work
+            n = rows_all
+            t1 = _ref_softmax_worker((n, el, 9, 1))
+            reps = max(1, min(100, int(5.0 / max(t1, 1e-3))))
+            t = _ref_softmax_worker((n, el, 9, reps))
+            cpu = {"value": reps * n * el * 8.0 / t / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference",
+                   "sample": f"reference host_softmax_forward (CPU fp32) on all {n} rows x {el}, {reps} "
+                             f"repetitions, {t:.1f} s on 1 core"}
         except FileNotFoundError as e:
             cpu = {"value": None, "unit": "GB/s", "cores": 1, "kind": "reference", "sample": f"unavailable: {e}"}
-    traffic = profile_traffic(args.workload)
+    traffic = profile_traffic(name)
     return {
-        "metric": "warp softmax GB/s (whole box)", "value": value, "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
+        "metric": SOFTMAX_METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": t_max / steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded N(0, 4) generated on device",
         "config": {"workload": wl[7], "rows": rows_all, "elements": el, "parallelism": f"row shards over {world} GPU(s)",
                    "l2": "256 MiB in + 256 MiB out per GPU at N=1 exceed the 126 MB L2; no flush"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": rows * el * 4,
                 "d2h_bytes_per_step": rows * el * 4, "api": "pmkl_warp_softmax_fwd (C ABI)", "steps": e2e_steps,
                 "chunks": n_chunks, "overlap": "H2D / softmax / D2H of consecutive row chunks on three streams"},
-        "gpu_launches": args.steps,
+        "gpu_launches": steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} copy bandwidth",
                      "traffic": (traffic * rows if traffic is not None else None),
@@ -696,6 +790,14 @@ def run_softmax(args, wl, rank, world, local):
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+
+
+RUNNERS = {"softmax": run_softmax, "attention-bwd": run_attention_bwd}
+
+
+def run_workload(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget):
+    fn = RUNNERS.get(name, run_attention)
+    return fn(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget)
 
 
 def main():
@@ -715,20 +817,39 @@ def main():
             print(json.dumps(line), flush=True)
         return
     rank, world, local = dist_init(args.gpus)
+    sampler = ClockSampler(local, not args.no_clocks)
     try:
-        if args.workload == "softmax":
-            line = run_softmax(args, wl, rank, world, local)
-        elif args.workload == "attention-bwd":
-            line = run_attention_bwd(args, wl, rank, world, local)
-        else:
-            line = run_attention(args, wl, rank, world, local)
+        line = run_workload(args, args.workload, wl, rank, world, local, sampler, args.steps, args.e2e_steps,
+                            20.0 if args.workload != "attention-bwd" else 15.0)
+        if sub_records_enabled(args):
+            # The other BASELINE workloads, measured the same way in the same
+            # run (device-timed value, roofline, end-to-end leg, CPU baseline,
+            # clocks), with their own step counts.
+            line["sub"] = {}
+            for key, name, min_steps, e2e_steps, budget in SUB_RECORDS:
+                rec = run_workload(args, name, WORKLOADS[name], rank, world, local, sampler,
+                                   max(args.steps, min_steps), e2e_steps, budget)
+                line["sub"][key] = rec
+                line["gpu_launches_all"] = line.get("gpu_launches_all", line["gpu_launches"]) + rec["gpu_launches"]
+        if world > 1:
+            # every rank's clocks; a throttled rank throttles the whole job
+            line["clocks_per_rank"] = gather_clocks(line.get("clocks"), world)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
+        sampler.stop()
         if world > 1:
             import torch.distributed as dist
 
             dist.destroy_process_group()
+
+
+def gather_clocks(clocks, world):
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, clocks)
+    return out
 
 
 if __name__ == "__main__":

@@ -170,24 +170,40 @@ int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k,
                                  int hidden, int dtype, int is_causal, float scale, void *workspace,
                                  size_t workspace_bytes, int kernel, void *stream);
 
-/* Workspace bytes pmkl_causal_attention_bwd needs for these sizes (enough for
- * either path; 0 for an empty problem).  No reference counterpart: the
- * reference's CPU backward needs no scratch. */
+/* Workspace bytes pmkl_causal_attention_bwd needs for these sizes (0 for an
+ * empty problem): on the tensor-core path the per-row statistics, 8 bytes per
+ * row at a row pitch of seq rounded up to 128; on the CUDA-core path 4 bytes
+ * per row.  No reference counterpart: the reference's CPU backward needs no
+ * scratch. */
 size_t pmkl_causal_attention_bwd_workspace_size(int batch, int heads, int seq, int hidden, int dtype);
 
+/* The same for pmkl_causal_attention_bwd_ex with a given kernel choice:
+ * PMKL_ATTN_TCGEN05_SIMPLE's long route also holds the forward's fp32 O, m, l
+ * (4 (hidden + 2) bytes more per row); 0 for an unknown choice.  No reference
+ * counterpart. */
+size_t pmkl_causal_attention_bwd_workspace_size_ex(int batch, int heads, int seq, int hidden, int dtype, int kernel);
+
 /* Size of the library's static device scratch used by
- * pmkl_causal_attention_bwd_static (64 MiB per device). */
+ * pmkl_causal_attention_bwd_static (64 MiB).  The array is a global of the
+ * library's device code, so every device on which the library's module is
+ * loaded holds it until the process exits, whichever entry points the caller
+ * uses. */
 #define PMKL_BWD_STATIC_SCRATCH_BYTES ((size_t)64 << 20)
 
 /*
  * pmkl_causal_attention_bwd without a caller workspace and without any device
  * allocation: the scratch is a statically allocated __device__ array of
- * PMKL_BWD_STATIC_SCRATCH_BYTES (256-byte aligned) inside libpmkl_b200, whose
- * address is looked up once per device.  No cudaMalloc, cudaFree or allocator
- * call happens on this path.  Same arguments (minus the workspace), results
+ * PMKL_BWD_STATIC_SCRATCH_BYTES (256-byte aligned) inside libpmkl_b200.  The
+ * first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current) and keeps it; a failed
+ * lookup returns PMKL_ERR_LAUNCH and is tried again on the next call.  Make
+ * that first call on each device before any stream capture.  No cudaMalloc,
+ * cudaFree or allocator call happens on this path.  Same arguments (minus the workspace), results
  * and status codes as pmkl_causal_attention_bwd; a problem whose
- * pmkl_causal_attention_bwd_workspace_size() exceeds the scratch is rejected
- * with PMKL_ERR_WORKSPACE before anything is launched.  Nothing in the scratch
+ * pmkl_causal_attention_bwd_workspace_size() exceeds the scratch (more than
+ * 8 Mi rows of batch x heads x seq rounded up to 128 on the tensor-core path,
+ * e.g. 512 (batch, head) slices of 16384 rows) is rejected with
+ * PMKL_ERR_WORKSPACE before anything is launched.  Nothing in the scratch
  * has to start at zero: every byte a kernel reads is written earlier in the
  * same call.
  *
@@ -239,6 +255,23 @@ int pmkl_stream_synchronize(void *stream);
  * (pmkl/core/launcher/cuda_launcher.h:297-335).
  */
 int pmkl_device_error(int clear);
+
+/*
+ * Bounded-wait self-test: launches `ctas` CTAs of a diagnostic kernel whose
+ * one waiting thread per CTA waits on an mbarrier that nothing ever arrives
+ * on, with a limit of `limit_ns` (100 us .. 2 s, the limit every kernel of
+ * this library uses).  It goes through the same steps as an attention kernel
+ * that gives up: the wait runs out, the CTA's abort flag is raised, issued
+ * tensor-core work is drained, tensor memory is freed and the device error
+ * word is set (read with pmkl_device_error).  A CTA that finds the word
+ * already set skips its work, as every tensor-core kernel does.  `out`
+ * (device memory, 2 * ctas values, 8-byte aligned) receives per CTA the
+ * outcome (0 completed, 1 ran out, 2 skipped) and the nanoseconds waited.
+ * Nothing faults, traps or hangs.  Diagnostic only; no reference counterpart
+ * (the reference checks errors on the host only,
+ * pmkl/core/utils/exception.h:121-129).
+ */
+int pmkl_wait_selftest(int ctas, unsigned long long limit_ns, unsigned long long *out, void *stream);
 
 /*
  * Tensor-core self-test: runs the tile primitives of the tcgen05 kernel in

@@ -70,6 +70,8 @@ def capi() -> ctypes.CDLL:
         L.pmkl_causal_attention_bwd_static.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp]
         L.pmkl_causal_attention_bwd_workspace_size.restype = ctypes.c_size_t
         L.pmkl_causal_attention_bwd_workspace_size.argtypes = [i32] * 5
+        L.pmkl_causal_attention_bwd_workspace_size_ex.restype = ctypes.c_size_t
+        L.pmkl_causal_attention_bwd_workspace_size_ex.argtypes = [i32] * 6
         L.pmkl_warp_softmax_fwd.restype = i32
         L.pmkl_warp_softmax_fwd.argtypes = [vp, vp] + [i32] * 6 + [vp]
         L.pmkl_status_string.restype = ctypes.c_char_p
@@ -80,6 +82,8 @@ def capi() -> ctypes.CDLL:
         L.pmkl_stream_synchronize.argtypes = [vp]
         L.pmkl_device_error.restype = i32
         L.pmkl_device_error.argtypes = [i32]
+        L.pmkl_wait_selftest.restype = i32
+        L.pmkl_wait_selftest.argtypes = [i32, ctypes.c_ulonglong, vp, vp]
         L.pmkl_tc_selftest.restype = i32
         L.pmkl_tc_selftest.argtypes = [i32, vp, vp, vp, i32, i32, vp]
         L.pmkl_attention_selected_kernel.restype = i32
@@ -134,8 +138,9 @@ def attention_fwd_strided(q, k, v, o, m, l, is_causal: bool, scale: float = 0.0,
         raise PmklError(rc, "pmkl_causal_attention_fwd_strided")
 
 
-def attention_bwd_workspace_size(B: int, H: int, S: int, D: int, dtype) -> int:
-    return int(capi().pmkl_causal_attention_bwd_workspace_size(B, H, S, D, torch_dtype_code(dtype)))
+def attention_bwd_workspace_size(B: int, H: int, S: int, D: int, dtype, kernel: int = KERNEL_AUTO) -> int:
+    """Workspace bytes of the backward route that ``kernel`` selects."""
+    return int(capi().pmkl_causal_attention_bwd_workspace_size_ex(B, H, S, D, torch_dtype_code(dtype), int(kernel)))
 
 
 def attention_bwd(dout, q, k, v, m, l, dq, dk, dv, is_causal: bool, scale: float = 0.0, kernel: int = KERNEL_AUTO,
@@ -148,7 +153,7 @@ def attention_bwd(dout, q, k, v, m, l, dq, dk, dv, is_causal: bool, scale: float
 
     B, H, S, D = q.shape
     if workspace is None:
-        workspace = torch.empty(max(attention_bwd_workspace_size(B, H, S, D, q.dtype), 1), dtype=torch.uint8,
+        workspace = torch.empty(max(attention_bwd_workspace_size(B, H, S, D, q.dtype, kernel), 1), dtype=torch.uint8,
                                 device=q.device)
     rc = capi().pmkl_causal_attention_bwd_ex(
         dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), m.data_ptr(), l.data_ptr(), dq.data_ptr(),

@@ -13,6 +13,8 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
+#include <atomic>
 #include <mutex>
 
 #include "attention_bwd.cuh"
@@ -23,6 +25,7 @@
 #include "common.cuh"
 #include "pmkl_b200.h"
 #include "softmax.cuh"
+#include "wait_selftest.cuh"
 
 // K+V bytes per scheduling group of the persistent attention kernel (tuned on
 // B200 at config 3: 24 MiB beat 48/96 MiB and no grouping).
@@ -342,6 +345,14 @@ int select_kernel(const void *q, const void *k, const void *v, const void *o, in
     const bool ready = hidden == 64 ? (bf ? pp_launchable<64, true>() : pp_launchable<64, false>())
                                     : (bf ? pp_launchable<128, true>() : pp_launchable<128, false>());
     if (ready) return PMKL_ATTN_TCGEN05;
+    // Only a build whose persistent kernel did not get its launch register
+    // count lands here; say so once, since the fallback costs ~40 %.
+    static std::once_flag warned;
+    std::call_once(warned, []() {
+        std::fprintf(stderr,
+                     "pmkl_b200: the persistent tensor-core attention kernel cannot take its register split in "
+                     "this build; falling back to a slower kernel (pmkl_attention_selected_kernel reports which)\n");
+    });
     return simple_ok ? PMKL_ATTN_TCGEN05_SIMPLE : PMKL_ATTN_SIMT;
 }
 
@@ -396,10 +407,15 @@ int attention_impl(const void *q, const void *k, const void *v, void *o, void *m
 // ------------------------------------------------------------------ backward
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// Workspace of the tensor-core backward: the forward's fp32 O, m, l, then the
-// per-row (b, delta) pairs at a row pitch of S rounded up to 128.
+// Workspace of the tensor-core backward: the per-row (b, delta) pairs at a
+// row pitch of S rounded up to 128 come first -- the fused route (delta from
+// the persistent forward's epilogue) needs nothing else -- followed by the
+// fp32 O, m, l that only the long route (a forward with fp32 outputs, then the
+// row-statistics kernel) writes.
 struct BwdLayout {
-    size_t o, m, l, rowstat, total;
+    size_t rowstat, o, m, l;
+    size_t fused_total;  // bytes the fused route needs
+    size_t total;        // bytes the long route needs
     int S_pad;
 };
 
@@ -407,14 +423,15 @@ BwdLayout bwd_layout_tc(long long BH, int S, int D) {
     BwdLayout L;
     L.S_pad = ((S + 127) / 128) * 128;
     size_t off = 0;
+    L.rowstat = off;
+    off = align256(off + static_cast<size_t>(BH) * L.S_pad * 8);
+    L.fused_total = off;
     L.o = off;
     off = align256(off + static_cast<size_t>(BH) * S * D * 4);
     L.m = off;
     off = align256(off + static_cast<size_t>(BH) * S * 4);
     L.l = off;
     off = align256(off + static_cast<size_t>(BH) * S * 4);
-    L.rowstat = off;
-    off = align256(off + static_cast<size_t>(BH) * L.S_pad * 8);
     L.total = off;
     return L;
 }
@@ -511,15 +528,13 @@ int launch_bwd_simt(const void *dout, const void *q, const void *k, const void *
 }
 
 // Scratch of pmkl_causal_attention_bwd_static: static device memory of this
-// module, never allocated or freed by a call.  Its address is looked up once
-// per device.
+// module, never allocated or freed by a call.  Every device on which the
+// module is loaded holds it, whichever entry points the caller uses.
 __device__ __align__(256) uint8_t g_bwd_static_scratch[PMKL_BWD_STATIC_SCRATCH_BYTES];
 
-struct StaticScratch {
-    std::once_flag once;
-    void *ptr = nullptr;
-};
-StaticScratch g_static_scratch[kMaxDevices];
+// Address of the scratch on each device, looked up with that device current.
+// Only a successful lookup is kept: a failed one is tried again next call.
+std::atomic<void *> g_static_scratch[kMaxDevices];
 
 void *static_scratch() {
     int dev = 0;
@@ -527,22 +542,26 @@ void *static_scratch() {
         cudaGetLastError();
         return nullptr;
     }
-    StaticScratch &s = g_static_scratch[dev];
-    std::call_once(s.once, [&]() {
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_bwd_static_scratch) == cudaSuccess)
-            s.ptr = p;
-        else
-            cudaGetLastError();
-    });
-    return s.ptr;
+    void *p = g_static_scratch[dev].load(std::memory_order_acquire);
+    if (p) return p;
+    if (cudaGetSymbolAddress(&p, g_bwd_static_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    g_static_scratch[dev].store(p, std::memory_order_release);
+    return p;
 }
 
-size_t bwd_workspace_size(long long BH, int S, int D, int dtype) {
+// Workspace bytes of the backward route that `kernel` selects for these sizes:
+// the fused tensor-core route (AUTO, TCGEN05) needs the row statistics only,
+// the long route (TCGEN05_SIMPLE) also the forward's fp32 O, m, l, and the
+// CUDA-core route one fp32 delta per row.
+size_t bwd_workspace_size(long long BH, int S, int D, int dtype, int kernel) {
     const bool tc_shape = (dtype == PMKL_DTYPE_F16 || dtype == PMKL_DTYPE_BF16) && (D == 64 || D == 128);
     const size_t simt_bytes = bwd_ws_simt(BH, S);
-    if (!tc_shape) return simt_bytes;
-    const size_t tc_bytes = bwd_layout_tc(BH, S, D).total;
+    if (!tc_shape || kernel == PMKL_ATTN_SIMT) return simt_bytes;
+    const BwdLayout L = bwd_layout_tc(BH, S, D);
+    const size_t tc_bytes = kernel == PMKL_ATTN_TCGEN05_SIMPLE ? L.total : L.fused_total;
     return tc_bytes > simt_bytes ? tc_bytes : simt_bytes;
 }
 
@@ -570,23 +589,26 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
     const void *const ptrs[9] = {dout, q, k, v, m, l, dq, dk, dv};
     const bool tc_ok = bwd_tc_applies(ptrs, hidden, dtype);
     if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
-    if (tc_ok && kernel != PMKL_ATTN_SIMT) {
-        const BwdLayout L = bwd_layout_tc(BH, seq, hidden);
-        if (workspace_bytes < L.total) return PMKL_ERR_WORKSPACE;
+    const bool bf = dtype == PMKL_DTYPE_BF16;
+    // delta = sum_j p dP comes from this library's forward through dO . O: the
+    // persistent kernel forms it in its epilogue (O never leaves tensor
+    // memory; the fused route); otherwise a forward with fp32 O, m, l and the
+    // row-statistics kernel (the long route, which needs the larger workspace).
+    const bool fused = tc_ok && kernel != PMKL_ATTN_TCGEN05_SIMPLE && kernel != PMKL_ATTN_SIMT &&
+                       (hidden == 64 ? (bf ? pp_launchable<64, true, true>() : pp_launchable<64, false, true>())
+                                     : (bf ? pp_launchable<128, true, true>() : pp_launchable<128, false, true>()));
+    const BwdLayout L = bwd_layout_tc(BH, seq, hidden);
+    // Without the fused route (a build whose persistent kernel cannot take its
+    // register split) the automatic choice takes the long route when the
+    // workspace holds it and the CUDA-core route otherwise, so that the size
+    // pmkl_causal_attention_bwd_workspace_size reports always suffices.
+    const bool tc_route = tc_ok && kernel != PMKL_ATTN_SIMT &&
+                          (fused || kernel != PMKL_ATTN_AUTO || workspace_bytes >= L.total);
+    if (tc_route) {
+        if (workspace_bytes < (fused ? L.fused_total : L.total)) return PMKL_ERR_WORKSPACE;
         uint8_t *ws = static_cast<uint8_t *>(workspace);
-        float *o32 = reinterpret_cast<float *>(ws + L.o);
-        float *m32 = reinterpret_cast<float *>(ws + L.m);
-        float *l32 = reinterpret_cast<float *>(ws + L.l);
         float2 *rowstat = reinterpret_cast<float2 *>(ws + L.rowstat);
-        // delta = sum_j p dP comes from this library's forward through dO . O:
-        // the persistent kernel forms it in its epilogue (O never leaves tensor
-        // memory); otherwise a forward with fp32 O, m, l and the row-statistics
-        // kernel.
         int rc;
-        const bool bf = dtype == PMKL_DTYPE_BF16;
-        const bool fused = kernel != PMKL_ATTN_TCGEN05_SIMPLE &&
-                           (hidden == 64 ? (bf ? pp_launchable<64, true, true>() : pp_launchable<64, false, true>())
-                                         : (bf ? pp_launchable<128, true, true>() : pp_launchable<128, false, true>()));
         if (fused) {
             const DeltaArgs da{dout, m, l, rowstat, L.S_pad};
             const AttnLayout lay = contiguous_layout(heads, seq, hidden);
@@ -600,6 +622,9 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
                            : launch_pp<128, false>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal,
                                                    sc, dtype, dtype, lay, stream, &da));
         } else {
+            float *o32 = reinterpret_cast<float *>(ws + L.o);
+            float *m32 = reinterpret_cast<float *>(ws + L.m);
+            float *l32 = reinterpret_cast<float *>(ws + L.l);
             rc = attention_impl(q, k, v, o32, m32, l32, batch, heads, seq, hidden, dtype, PMKL_DTYPE_F32, causal, sc,
                                 kernel == PMKL_ATTN_TCGEN05_SIMPLE ? PMKL_ATTN_TCGEN05_SIMPLE : PMKL_ATTN_AUTO,
                                 stream_);
@@ -741,8 +766,16 @@ int pmkl_causal_attention_bwd_static(const void *dout, const void *q, const void
 }
 
 size_t pmkl_causal_attention_bwd_workspace_size(int batch, int heads, int seq, int hidden, int dtype) {
+    return pmkl_causal_attention_bwd_workspace_size_ex(batch, heads, seq, hidden, dtype, PMKL_ATTN_AUTO);
+}
+
+size_t pmkl_causal_attention_bwd_workspace_size_ex(int batch, int heads, int seq, int hidden, int dtype,
+                                                   int kernel) {
     if (batch <= 0 || heads <= 0 || seq <= 0 || hidden <= 0 || !dtype_valid(dtype)) return 0;
-    return bwd_workspace_size(static_cast<long long>(batch) * heads, seq, hidden, dtype);
+    if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
+        kernel != PMKL_ATTN_TCGEN05_SIMPLE)
+        return 0;
+    return bwd_workspace_size(static_cast<long long>(batch) * heads, seq, hidden, dtype, kernel);
 }
 
 int pmkl_causal_attention_fwd_strided(const void *q, const void *k, const void *v, void *o, void *m, void *l,
@@ -852,6 +885,17 @@ int pmkl_device_error(int clear) {
         if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess) return PMKL_ERR_LAUNCH;
     }
     return word ? PMKL_ERR_DEVICE_TIMEOUT : PMKL_OK;
+}
+
+int pmkl_wait_selftest(int ctas, unsigned long long limit_ns, unsigned long long *out, void *stream) {
+    if (ctas < 1 || ctas > 1024) return PMKL_ERR_INVALID_SHAPE;
+    if (limit_ns < 100000ull || limit_ns > ptx::kWaitTimeoutNs) return PMKL_ERR_INVALID_SHAPE;
+    if (!out) return PMKL_ERR_NULL_POINTER;
+    if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return PMKL_ERR_MISALIGNED;
+    const int dev_rc = current_device_ok();
+    if (dev_rc != PMKL_OK) return dev_rc;
+    diag::wait_selftest_kernel<<<ctas, 128, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, out);
+    return launch_status();
 }
 
 int pmkl_tc_selftest(int which, const void *a, const void *b, float *c, int hidden, int dtype, void *stream_) {

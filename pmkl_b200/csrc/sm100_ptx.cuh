@@ -74,17 +74,19 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t pa
 }
 
 // Waits for the phase with the given parity to complete.  Returns false when
-// the CTA-wide abort flag is raised or the wait exceeds kWaitTimeoutNs (in
-// which case this call raises the abort flag itself).  Single-thread form.
-// Each try_wait parks the thread for at most kSuspendHintNs, so the abort
-// flag and the deadline are checked at least that often.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+// the CTA-wide abort flag is raised or the wait exceeds limit_ns (in which
+// case this call raises the abort flag itself).  Single-thread form.  Each
+// try_wait parks the thread for at most kSuspendHintNs, so the abort flag and
+// the deadline are checked at least that often.  The kernels use the default
+// limit; the wait self-test passes a short one.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          unsigned long long limit_ns = kWaitTimeoutNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     for (;;) {
         if (mbar_try_wait_suspend(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
+        if (globaltimer() - t0 > limit_ns) {
             *abort_flag = 1;
             return false;
         }

@@ -129,7 +129,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> backward_impl(const at::Tensor &d
     // Every element is written, so empty (not zeros, :186-188) gives the same result.
     at::Tensor dq = at::empty_like(q), dk = at::empty_like(k), dv = at::empty_like(v);
     const int dt = pmkl_dtype_of(v.scalar_type());
-    const size_t ws_bytes = pmkl_causal_attention_bwd_workspace_size(B, H, S, D, dt);
+    const size_t ws_bytes = pmkl_causal_attention_bwd_workspace_size_ex(B, H, S, D, dt, static_cast<int>(kernel));
     at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes > 0 ? ws_bytes : 1)}, q.options().dtype(at::kByte));
     cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
     const int rc = pmkl_causal_attention_bwd_ex(dc.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),

@@ -237,4 +237,10 @@ def test_errors():
     assert call(ws.data_ptr(), need, kernel=3, dtype=0) == -5  # fp32 has no tensor-core path
     assert call(ws.data_ptr(), need, kernel=TC, dtype=0) == -5  # fp32 has no tensor-core path
     assert call(ws.data_ptr(), need) == 0
+    # the long route (PMKL_ATTN_TCGEN05_SIMPLE) needs its own, larger size
+    need3 = pmkl_b200.attention_bwd_workspace_size(1, 1, 64, 64, torch.bfloat16, kernel=3)
+    assert need3 > need
+    ws3 = torch.empty(need3, dtype=torch.uint8, device="cuda")
+    assert call(ws3.data_ptr(), need, kernel=3) == -9
+    assert call(ws3.data_ptr(), need3, kernel=3) == 0
     torch.cuda.synchronize()

@@ -93,21 +93,49 @@ def test_backward_argument_errors():
 
 
 def test_backward_workspace_size():
-    """Tensor-core layout: fp32 O, m, l of the forward plus (b, delta) pairs at a
-    row pitch of seq rounded up to 128, each region 256-byte aligned; the
-    CUDA-core path needs one fp32 delta per row."""
+    """Tensor-core path: the automatic (fused) route needs the (b, delta) pairs
+    only, at a row pitch of seq rounded up to 128; the long route
+    (PMKL_ATTN_TCGEN05_SIMPLE) adds the forward's fp32 O, m, l, each region
+    256-byte aligned.  The CUDA-core path needs one fp32 delta per row."""
     L = pmkl_b200.capi()
     f = L.pmkl_causal_attention_bwd_workspace_size
+    fx = L.pmkl_causal_attention_bwd_workspace_size_ex
     a = lambda x: (x + 255) // 256 * 256  # noqa: E731
     B, H, S, D = 2, 3, 200, 128
     BH = B * H
-    assert f(B, H, S, D, 2) == a(BH * S * D * 4) + 2 * a(BH * S * 4) + a(BH * 256 * 8)
-    assert f(B, H, S, 64, 1) == a(BH * S * 64 * 4) + 2 * a(BH * S * 4) + a(BH * 256 * 8)
+    fused = a(BH * 256 * 8)
+    assert f(B, H, S, D, 2) == fused
+    assert fx(B, H, S, D, 2, 0) == fused and fx(B, H, S, D, 2, 2) == fused
+    assert fx(B, H, S, D, 2, 3) == fused + a(BH * S * D * 4) + 2 * a(BH * S * 4)
+    assert fx(B, H, S, 64, 1, 3) == fused + a(BH * S * 64 * 4) + 2 * a(BH * S * 4)
+    assert fx(B, H, S, D, 2, 1) == a(BH * S * 4)  # CUDA-core route
+    assert fx(B, H, S, D, 2, 9) == 0  # unknown choice
     assert f(B, H, S, 96, 2) == a(BH * S * 4)  # no tensor-core path for D = 96
     assert f(B, H, S, D, 0) == a(BH * S * 4)  # fp32
     assert f(0, H, S, D, 2) == 0 and f(B, H, 0, D, 2) == 0 and f(B, H, S, D, 9) == 0
-    # config 3 (bf16 B16 H32 S4096 D128): about 1.1 GB
-    assert 1.0e9 < f(16, 32, 4096, 128, 2) < 1.2e9
+    # config 3 (bf16 B16 H32 S4096 D128): 16 MiB, within the static scratch
+    assert f(16, 32, 4096, 128, 2) == 16 << 20
+    assert f(16, 32, 4096, 128, 2) <= 64 << 20
+
+
+def test_static_scratch_limit_sizes():
+    """The sizes the no-allocation backward's 64 MiB scratch admits on the
+    tensor-core route: 2048 slices of 4096 rows fit exactly, 2049 do not (the
+    GPU test of that entry point uses both)."""
+    L = pmkl_b200.capi()
+    f = L.pmkl_causal_attention_bwd_workspace_size
+    assert f(1, 2048, 4096, 64, 2) == 64 << 20
+    assert f(1, 2049, 4096, 64, 2) > 64 << 20
+
+
+def test_wait_selftest_argument_errors():
+    L = pmkl_b200.capi()
+    f = L.pmkl_wait_selftest
+    assert f(0, 5_000_000, 0x10000, None) == -1  # no CTA
+    assert f(2, 10, 0x10000, None) == -1  # limit below 100 us
+    assert f(2, 3_000_000_000, 0x10000, None) == -1  # limit above the 2 s every kernel uses
+    assert f(2, 5_000_000, 0, None) == -3
+    assert f(2, 5_000_000, 0x10004, None) == -4
 
 
 def test_strided_argument_errors():

@@ -6,6 +6,8 @@ other test has used the device (and its caching allocator); they also pass on
 their own.  Each compares the static entry point with
 pmkl_causal_attention_bwd (caller workspace) on the same inputs, bit for bit,
 over several calls in a row."""
+import gc
+
 import pytest
 import torch
 
@@ -27,6 +29,17 @@ def _no_device_timeouts():
 def make_problem(B, H, S, D, dtype, seed, causal):
     q, k, v = (t.cuda() for t in seeded_qkv(B, H, S, D, dtype, seed=seed))
     do = torch.randn(q.shape, generator=torch.Generator().manual_seed(seed + 1)).to(dtype).cuda()
+    o = torch.empty_like(q)
+    m = torch.empty(B, H, S, dtype=dtype, device="cuda")
+    l = torch.empty_like(m)
+    pmkl_b200.attention_fwd(q, k, v, o, m, l, causal)
+    return do, q, k, v, m, l
+
+
+def make_problem_on_device(B, H, S, D, dtype, seed, causal):
+    """As make_problem, with the inputs drawn on the device (large sizes)."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q, k, v, do = (torch.randn(B, H, S, D, generator=g, device="cuda").to(dtype) for _ in range(4))
     o = torch.empty_like(q)
     m = torch.empty(B, H, S, dtype=dtype, device="cuda")
     l = torch.empty_like(m)
@@ -92,37 +105,64 @@ def test_no_device_memory_is_allocated():
     assert rc == 0
     torch.cuda.synchronize()
     grads = [torch.empty_like(p[1]) for _ in range(3)]
-    free0, _ = torch.cuda.mem_get_info()
-    alloc0 = torch.cuda.memory_allocated()
-    reserved0 = torch.cuda.memory_reserved()
-    B, H, S, D = p[1].shape
-    for _ in range(3):
-        rc = pmkl_b200.capi().pmkl_causal_attention_bwd_static(
-            *(t.data_ptr() for t in p), *(g.data_ptr() for g in grads), B, H, S, D, CODE[p[1].dtype], 0, 0.0,
-            torch.cuda.current_stream().cuda_stream)
-        assert rc == 0
-    torch.cuda.synchronize()
-    assert torch.cuda.mem_get_info()[0] == free0
-    assert torch.cuda.memory_allocated() == alloc0 and torch.cuda.memory_reserved() == reserved0
+    # torch's allocator counters of this process (the device-wide free memory
+    # would also move with other processes on a shared GPU).  Tensors left
+    # unreachable by earlier tests are collected first, and the collector is
+    # off during the calls, so that only these calls could move the counters.
+    gc.collect()
+    gc.disable()
+    try:
+        alloc0 = torch.cuda.memory_allocated()
+        reserved0 = torch.cuda.memory_reserved()
+        B, H, S, D = p[1].shape
+        for _ in range(3):
+            rc = pmkl_b200.capi().pmkl_causal_attention_bwd_static(
+                *(t.data_ptr() for t in p), *(g.data_ptr() for g in grads), B, H, S, D, CODE[p[1].dtype], 0, 0.0,
+                torch.cuda.current_stream().cuda_stream)
+            assert rc == 0
+        torch.cuda.synchronize()
+        assert torch.cuda.memory_allocated() == alloc0 and torch.cuda.memory_reserved() == reserved0
+    finally:
+        gc.enable()
 
 
 def test_oversize_problem_is_rejected_without_launch():
-    B, H, S, D = 1, 32, 4096, 128  # needs 69.2 MB > 64 MiB
-    assert pmkl_b200.attention_bwd_workspace_size(B, H, S, D, torch.bfloat16) > STATIC_BYTES
+    """The tensor-core route needs 8 bytes per row at a row pitch of seq
+    rounded up to 128: 2049 slices of 4096 rows exceed the 64 MiB scratch and
+    are refused before any launch; 2048 slices fill it exactly and run."""
+    B, S, D = 1, 4096, 64
+    assert pmkl_b200.attention_bwd_workspace_size(B, 2049, S, D, torch.bfloat16) > STATIC_BYTES
     x = torch.zeros(1, dtype=torch.bfloat16, device="cuda")
     ptr = x.data_ptr()
-    rc = pmkl_b200.capi().pmkl_causal_attention_bwd_static(*([ptr] * 9), B, H, S, D, 2, 1, 0.0, None)
+    rc = pmkl_b200.capi().pmkl_causal_attention_bwd_static(*([ptr] * 9), B, 2049, S, D, 2, 1, 0.0, None)
     assert rc == -9  # PMKL_ERR_WORKSPACE
-    # the largest problem of that shape family that fits runs
-    H_fit = 31  # 67.0 MB
-    assert pmkl_b200.attention_bwd_workspace_size(B, H_fit, S, D, torch.bfloat16) <= STATIC_BYTES
-    p = make_problem(B, H_fit, S, D, torch.bfloat16, 7, True)
+    H_fit = 2048
+    assert pmkl_b200.attention_bwd_workspace_size(B, H_fit, S, D, torch.bfloat16) == STATIC_BYTES
+    p = make_problem_on_device(B, H_fit, S, D, torch.bfloat16, 7, True)
     rc, got = bwd_static(*p, True)
-    assert rc == 0
+    assert rc == 0, pmkl_b200.capi().pmkl_status_string(rc)
     ref = bwd_workspace(*p, True)
     torch.cuda.synchronize()
     for a, b in zip(got, ref):
         assert torch.equal(a, b)
+    del p, got, ref
+    torch.cuda.empty_cache()
+
+
+def test_config3_size_runs_from_the_static_scratch():
+    """BASELINE config 3's shape (bf16 B16 H32 S4096 D128) needs 16 MiB of
+    row statistics and runs from the static scratch, bit for bit like the
+    workspace entry point, twice in a row."""
+    p = make_problem_on_device(16, 32, 4096, 128, torch.bfloat16, 8, True)
+    ref = bwd_workspace(*p, True)
+    for _ in range(2):
+        rc, got = bwd_static(*p, True)
+        assert rc == 0, pmkl_b200.capi().pmkl_status_string(rc)
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)
+    del p, got, ref
+    torch.cuda.empty_cache()
 
 
 def test_argument_errors_match_workspace_entry():
