@@ -99,7 +99,10 @@ struct Params {
     long long o_sb, o_sh, o_ss;  // element strides of O (batch, head, row) for fp32 output
     int n_pairs;     // ceil(n_qt / 2)
     int n_units;     // n_pairs * BH
+    int n_rounds;    // ceil(n_units / gridDim.x)
     int group;       // (b, h) slices per scheduling group
+    int snake;       // odd rounds go to the CTAs in reverse order
+    int flip;        // odd groups run their pairs shortest first
     int causal;
     int out_dtype;
     float scale;
@@ -132,9 +135,10 @@ struct Unit {
 
 // Work order: slices are taken in groups of p.group (b, h) slices whose K and
 // V together fit in L2, and inside a group the query-tile pairs go longest
-// first.  All pairs of a slice then run close together in time and re-read
-// that slice's K/V from L2 instead of HBM, while the longest-first order keeps
-// the CTAs' loads balanced.
+// first (with p.flip, every other group shortest first, so that a CTA that
+// drew long pairs in one group draws short ones in the next).  All pairs of a
+// slice then run close together in time and re-read that slice's K/V from L2
+// instead of HBM.
 __device__ __forceinline__ Unit decode(const Params &p, int u) {
     Unit w;
     const int n_kv_all = (p.S + 127) / 128;
@@ -142,9 +146,10 @@ __device__ __forceinline__ Unit decode(const Params &p, int u) {
     const int g = u / per_group;
     const int within = u - g * per_group;
     const int g_slices = min(p.group, p.BH - g * p.group);
-    const int rank = within / g_slices;
+    const int rank0 = within / g_slices;
+    const int rank = (p.flip && (g & 1)) ? (p.n_pairs - 1 - rank0) : rank0;
     const int pair = p.causal ? (p.n_pairs - 1 - rank) : rank;
-    w.bh = g * p.group + (within - rank * g_slices);
+    w.bh = g * p.group + (within - rank0 * g_slices);
     w.row0 = pair * 256;
     for (int x = 0; x < 2; ++x) {
         const int r0 = w.row0 + 128 * x;
@@ -154,6 +159,16 @@ __device__ __forceinline__ Unit decode(const Params &p, int u) {
     }
     w.n_max = max(w.n[0], w.n[1]);
     return w;
+}
+
+// The list entry a CTA takes in round k: rounds of gridDim.x consecutive
+// entries, one per CTA; with p.snake, odd rounds hand them out in reverse CTA
+// order, so that over a longest-first list every CTA alternates between the
+// long and the short end of a round.  Returns n_units or more for a CTA that
+// has no entry in the (last, partial) round.
+__device__ __forceinline__ int unit_of(const Params &p, int k) {
+    const int b = (p.snake && (k & 1)) ? static_cast<int>(gridDim.x - 1 - blockIdx.x) : static_cast<int>(blockIdx.x);
+    return k * static_cast<int>(gridDim.x) + b;
 }
 
 // 2^x for x <= 0 on the FMA pipe, two lanes per instruction, to take load off
@@ -350,7 +365,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t qc0 = 0, qc1 = 0;
             int kvc = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+            for (int k = 0; ok && k < p.n_rounds; ++k) {
+                const int u = unit_of(p, k);
+                if (u >= p.n_units) continue;
                 const Unit w = decode(p, u);
                 const int bb = w.bh / p.H;
                 const int hh = w.bh - bb * p.H;
@@ -442,7 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mma_ts_h(d, a + kPLo + kk * 8, b0 + static_cast<uint32_t>(kk * 128), v_hi, kIdescO, 1u);
                 }
             };
-            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+            for (int k = 0; ok && k < p.n_rounds; ++k) {
+                const int u = unit_of(p, k);
+                if (u >= p.n_units) continue;
                 const Unit w = decode(p, u);
                 const int n0 = w.n[0], n1 = w.n[1];
                 const bool hl0 = w.hilo[0], hl1 = w.hilo[1];
@@ -567,7 +586,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             int sc = 0, uc = 0;
             uint32_t pvc = 0;  // head size 64: P tiles stored so far (one P.V each)
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+            for (int k = 0; ok && k < p.n_rounds; ++k) {
+                const int u = unit_of(p, k);
+                if (u >= p.n_units) continue;
                 const Unit w = decode(p, u);
                 // This warpgroup's tile, picked by value (no run-time array index).
                 const bool actx = x ? w.act[1] : w.act[0];
@@ -736,7 +757,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t oc0 = 0, oc1 = 0;
             int nb = 0;  // staging boxes used so far
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+            for (int k = 0; ok && k < p.n_rounds; ++k) {
+                const int u = unit_of(p, k);
+                if (u >= p.n_units) continue;
                 const Unit w = decode(p, u);
                 for (int x = 0; x < 2 && ok; ++x) {
                     if (!(x ? w.act[1] : w.act[0])) continue;

@@ -101,7 +101,7 @@ def test_two_static_calls_in_a_row_before_reading():
 
 def test_no_device_memory_is_allocated():
     p = make_problem(*CASES[1])
-    rc, _ = bwd_static(*p, False)  # first call: module and scratch address set-up
+    rc, first = bwd_static(*p, False)  # first call: module and scratch address set-up
     assert rc == 0
     torch.cuda.synchronize()
     grads = [torch.empty_like(p[1]) for _ in range(3)]
@@ -115,7 +115,7 @@ def test_no_device_memory_is_allocated():
         alloc0 = torch.cuda.memory_allocated()
         reserved0 = torch.cuda.memory_reserved()
         B, H, S, D = p[1].shape
-        for _ in range(3):
+        for _call in range(3):
             rc = pmkl_b200.capi().pmkl_causal_attention_bwd_static(
                 *(t.data_ptr() for t in p), *(g.data_ptr() for g in grads), B, H, S, D, CODE[p[1].dtype], 0, 0.0,
                 torch.cuda.current_stream().cuda_stream)
@@ -124,6 +124,8 @@ def test_no_device_memory_is_allocated():
         assert torch.cuda.memory_allocated() == alloc0 and torch.cuda.memory_reserved() == reserved0
     finally:
         gc.enable()
+    for a, b in zip(first, grads):  # the calls also agree with each other
+        assert torch.equal(a, b)
 
 
 def test_oversize_problem_is_rejected_without_launch():
