@@ -203,7 +203,7 @@ def dist_init(n_gpus: int):
         raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     return rank, world, local
 
 

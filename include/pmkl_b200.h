@@ -170,6 +170,36 @@ int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k,
                                  int hidden, int dtype, int is_causal, float scale, void *workspace,
                                  size_t workspace_bytes, int kernel, void *stream);
 
+/*
+ * As pmkl_causal_attention_bwd_ex for strided and grouped-query tensors, the
+ * backward of pmkl_causal_attention_fwd_strided: views (e.g. [batch, seq,
+ * heads, hidden] tensors seen as [batch, heads, seq, hidden]) are read and the
+ * gradients written in place, with no copies; the reference makes its inputs
+ * contiguous (fused_self_attention.cpp:160-162, :179) and takes equal head
+ * counts only (:178-180).
+ *
+ *   dout, q, dq : [batch, heads, seq, hidden] at b * s[0] + h * s[1] + row * s[2]
+ *                 + col (element strides dout_strides, q_strides, dq_strides;
+ *                 the hidden dimension contiguous).
+ *   k, v, dk, dv: the same with kv_heads heads; query head h reads K/V head
+ *                 h / (heads / kv_heads), and dk, dv are the sums over those
+ *                 query heads (formed in fp32, rounded once).
+ *   m, l        : contiguous [batch, heads, seq].
+ *   a NULL strides pointer means that tensor is contiguous.
+ * Workspace as for pmkl_causal_attention_bwd with the query heads
+ * (pmkl_causal_attention_bwd_workspace_size(batch, heads, ...)).  The
+ * tensor-core path runs when the pointers are 16-byte aligned and every stride
+ * is a multiple of 16 bytes; otherwise the CUDA-core path.  kv_heads that does
+ * not divide heads or negative strides give PMKL_ERR_INVALID_SHAPE;
+ * PMKL_ATTN_TCGEN05_SIMPLE accepts contiguous, equal-head tensors only.
+ */
+int pmkl_causal_attention_bwd_strided(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                                      const void *l, void *dq, void *dk, void *dv, int batch, int heads, int kv_heads,
+                                      int seq, int hidden, const int64_t *dout_strides, const int64_t *q_strides,
+                                      const int64_t *k_strides, const int64_t *v_strides, const int64_t *dq_strides,
+                                      const int64_t *dk_strides, const int64_t *dv_strides, int dtype, int is_causal,
+                                      float scale, void *workspace, size_t workspace_bytes, int kernel, void *stream);
+
 /* Workspace bytes pmkl_causal_attention_bwd needs for these sizes (0 for an
  * empty problem): on the tensor-core path the per-row statistics, 8 bytes per
  * row at a row pitch of seq rounded up to 128; on the CUDA-core path 4 bytes

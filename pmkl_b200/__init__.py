@@ -66,6 +66,9 @@ def capi() -> ctypes.CDLL:
         L.pmkl_causal_attention_bwd.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp, ctypes.c_size_t, vp]
         L.pmkl_causal_attention_bwd_ex.restype = i32
         L.pmkl_causal_attention_bwd_ex.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp, ctypes.c_size_t, i32, vp]
+        L.pmkl_causal_attention_bwd_strided.restype = i32
+        L.pmkl_causal_attention_bwd_strided.argtypes = [vp] * 9 + [i32] * 5 + [i64p] * 7 + [i32] * 2 + [
+            f32, vp, ctypes.c_size_t, i32, vp]
         L.pmkl_causal_attention_bwd_static.restype = i32
         L.pmkl_causal_attention_bwd_static.argtypes = [vp] * 9 + [i32] * 6 + [f32, vp]
         L.pmkl_causal_attention_bwd_workspace_size.restype = ctypes.c_size_t
@@ -161,6 +164,32 @@ def attention_bwd(dout, q, k, v, m, l, dq, dk, dv, is_causal: bool, scale: float
         workspace.data_ptr(), workspace.numel(), int(kernel), _stream_ptr(stream))
     if rc != PMKL_OK:
         raise PmklError(rc, "pmkl_causal_attention_bwd")
+
+
+def attention_bwd_strided(dout, q, k, v, m, l, dq, dk, dv, is_causal: bool, scale: float = 0.0,
+                          kernel: int = KERNEL_AUTO, workspace=None, stream=None) -> None:
+    """pmkl_causal_attention_bwd_strided on torch CUDA tensors of logical shape
+    [B, H, S, D] (dout, q, dq) and [B, H_kv, S, D] (k, v, dk, dv) with any
+    strides whose last dimension is contiguous; m, l contiguous [B, H, S]."""
+    import torch
+
+    B, H, S, D = q.shape
+    Hkv = k.shape[1]
+
+    def st(t):
+        assert t.stride(3) == 1 or t.shape[3] <= 1, "the hidden dimension must be contiguous"
+        return (ctypes.c_int64 * 3)(t.stride(0), t.stride(1), t.stride(2))
+
+    if workspace is None:
+        workspace = torch.empty(max(attention_bwd_workspace_size(B, H, S, D, q.dtype, kernel), 1), dtype=torch.uint8,
+                                device=q.device)
+    rc = capi().pmkl_causal_attention_bwd_strided(
+        dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), m.data_ptr(), l.data_ptr(), dq.data_ptr(),
+        dk.data_ptr(), dv.data_ptr(), B, H, Hkv, S, D, st(dout), st(q), st(k), st(v), st(dq), st(dk), st(dv),
+        torch_dtype_code(q.dtype), int(bool(is_causal)), float(scale), workspace.data_ptr(), workspace.numel(),
+        int(kernel), _stream_ptr(stream))
+    if rc != PMKL_OK:
+        raise PmklError(rc, "pmkl_causal_attention_bwd_strided")
 
 
 KERNEL_NAMES = {KERNEL_SIMT: "attn_fwd_simt_kernel", KERNEL_TCGEN05: "attn_fwd_pp_kernel",

@@ -20,9 +20,13 @@
 //   2. attn_bwd_dq_kernel: one CTA per (slice, 128-row query tile); per key
 //      tile S = Q K^T and dP = dO V^T into tensor memory, dS (16-bit) back
 //      into tensor memory, dQ += dS K.
-//   3. attn_bwd_dkv_kernel: one CTA per (slice, 128-row key tile); per query
-//      tile S^T = K Q^T and dP^T = V dO^T, P^T and dS^T (16-bit) back into
-//      tensor memory, dV += P^T dO and dK += dS^T Q.
+//   3. attn_bwd_dkv_kernel: one CTA per (K/V slice, 128-row key tile); per
+//      query tile of every query head that reads this K/V head (grouped-query
+//      attention: kv_group heads, one after the other) S^T = K Q^T and
+//      dP^T = V dO^T, P^T and dS^T (16-bit) back into tensor memory,
+//      dV += P^T dO and dK += dS^T Q, summed over the group in tensor memory.
+// Every tensor is addressed through 4-D maps {D, S, heads, batch} with the
+// caller's strides, so views are read and written in place.
 // Both gradient kernels: warps 0-7 are the elementwise warps (two per tile
 // row -- one per half of the columns; the backward's elementwise work has no
 // row reduction), warp 8 issues TMA loads, warp 9 (one thread) issues
@@ -63,7 +67,10 @@ constexpr int kStatBytes = 128 * 8;  // (b, delta) of one 128-row query tile
 struct Params {
     int S;
     int S_pad;   // row pitch of the row statistics (a multiple of 128)
-    int BH;
+    int BH;      // query slices: batch x heads
+    int H;       // query heads; slice bh = b H + h
+    int kv_group;  // query heads per K/V head: query head h reads K/V head h / kv_group
+    int BHkv;    // K/V slices: batch x heads / kv_group
     int n_qt;    // 128-row tiles per slice
     int causal;
     float scale;
@@ -186,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int bid = blockIdx.x;
     const int qt = p.causal ? (p.n_qt - 1 - bid / p.BH) : (bid / p.BH);  // heaviest tiles first
     const int bh = bid % p.BH;
+    const int bb = bh / p.H, hh = bh - bb * p.H, hkv = hh / p.kv_group;
     const int n_kv = p.causal ? qt + 1 : p.n_qt;
 
     if (threadIdx.x == 0) {
@@ -228,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tm_do);
             mbar_arrive_expect_tx(qd_full, 2 * TILE);
             for (int b = 0; b < C::kBoxes; ++b) {
-                tma_load_3d(sQ + b * kBoxBytes, &tm_q, qd_full, b * kBoxCols, qt * 128, bh);
-                tma_load_3d(sDO + b * kBoxBytes, &tm_do, qd_full, b * kBoxCols, qt * 128, bh);
+                tma_load_4d(sQ + b * kBoxBytes, &tm_q, qd_full, b * kBoxCols, qt * 128, hh, bb);
+                tma_load_4d(sDO + b * kBoxBytes, &tm_do, qd_full, b * kBoxCols, qt * 128, hh, bb);
             }
             int issued = 0;
             for (int t = 0; t < n_kv; ++t) {
@@ -237,14 +245,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (t >= KS && !mbar_wait(&k_empty[sk], ((t / KS) - 1) & 1, abort_flag)) break;
                 mbar_arrive_expect_tx(&k_full[sk], TILE);
                 for (int b = 0; b < C::kBoxes; ++b)
-                    tma_load_3d(sK + sk * TILE + b * kBoxBytes, &tm_k, &k_full[sk], b * kBoxCols, t * 128, bh);
+                    tma_load_4d(sK + sk * TILE + b * kBoxBytes, &tm_k, &k_full[sk], b * kBoxCols, t * 128, hkv, bb);
                 if (t >= VS && !mbar_wait(&v_empty[sv], ((t / VS) - 1) & 1, abort_flag)) {
                     issued = -(t + 1);  // K(t) issued, V(t) not
                     break;
                 }
                 mbar_arrive_expect_tx(&v_full[sv], TILE);
                 for (int b = 0; b < C::kBoxes; ++b)
-                    tma_load_3d(sV + sv * TILE + b * kBoxBytes, &tm_v, &v_full[sv], b * kBoxCols, t * 128, bh);
+                    tma_load_4d(sV + sv * TILE + b * kBoxBytes, &tm_v, &v_full[sv], b * kBoxCols, t * 128, hkv, bb);
                 issued = t + 1;
             }
             if (*abort_flag) {
@@ -404,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(staged);
             if (threadIdx.x == 0 && mbar_wait(staged, 0, abort_flag)) {
                 for (int bx = 0; bx < C::kBoxes; ++bx)
-                    tma_store_3d(&tm_dq, sQ + bx * kBoxBytes, bx * kBoxCols, qt * 128, bh);
+                    tma_store_4d(&tm_dq, sQ + bx * kBoxBytes, bx * kBoxCols, qt * 128, hh, bb);
                 tma_store_commit();
                 tma_store_wait_read0();
             }
@@ -473,10 +481,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int bid = blockIdx.x;
-    const int kt = bid / p.BH;  // causal: key tile 0 meets every query tile, so ascending = heaviest first
-    const int bh = bid % p.BH;
+    const int kt = bid / p.BHkv;  // causal: key tile 0 meets every query tile, so ascending = heaviest first
+    const int bkv = bid % p.BHkv;
+    const int Hkv = p.H / p.kv_group;
+    const int bb = bkv / Hkv, hkv = bkv - bb * Hkv;
     const int i0 = p.causal ? kt : 0;
-    const int n_q = p.n_qt - i0;
+    const int n_q = p.n_qt - i0;     // query tiles per query head
+    const int n_x = n_q * p.kv_group;  // (query head of the group, query tile) steps
 
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
@@ -514,22 +525,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tm_do);
             mbar_arrive_expect_tx(kv_full, 2 * TILE);
             for (int b = 0; b < C::kBoxes; ++b) {
-                tma_load_3d(sK + b * kBoxBytes, &tm_k, kv_full, b * kBoxCols, kt * 128, bh);
-                tma_load_3d(sV + b * kBoxBytes, &tm_v, kv_full, b * kBoxCols, kt * 128, bh);
+                tma_load_4d(sK + b * kBoxBytes, &tm_k, kv_full, b * kBoxCols, kt * 128, hkv, bb);
+                tma_load_4d(sV + b * kBoxBytes, &tm_v, kv_full, b * kBoxCols, kt * 128, hkv, bb);
             }
             int issued = 0;
-            for (int x = 0; x < n_q; ++x) {
+            for (int x = 0; x < n_x; ++x) {
                 const int s = x % NS;
-                const int i = i0 + x;
+                const int g = x / n_q;
+                const int i = i0 + (x - g * n_q);
+                const int hh = hkv * p.kv_group + g;  // query head
                 if (x >= NS && !mbar_wait(&qd_empty[s], ((x / NS) - 1) & 1, abort_flag)) break;
                 uint8_t *st = sRing + s * STAGE;
                 mbar_arrive_expect_tx(&qd_full[s], 2 * TILE + kStatBytes);
                 for (int b = 0; b < C::kBoxes; ++b) {
-                    tma_load_3d(st + b * kBoxBytes, &tm_q, &qd_full[s], b * kBoxCols, i * 128, bh);
-                    tma_load_3d(st + TILE + b * kBoxBytes, &tm_do, &qd_full[s], b * kBoxCols, i * 128, bh);
+                    tma_load_4d(st + b * kBoxBytes, &tm_q, &qd_full[s], b * kBoxCols, i * 128, hh, bb);
+                    tma_load_4d(st + TILE + b * kBoxBytes, &tm_do, &qd_full[s], b * kBoxCols, i * 128, hh, bb);
                 }
-                bulk_load(st + 2 * TILE, p.rowstat + static_cast<size_t>(bh) * p.S_pad + i * 128, kStatBytes,
-                          &qd_full[s]);
+                bulk_load(st + 2 * TILE,
+                          p.rowstat + static_cast<size_t>(bb * p.H + hh) * p.S_pad + static_cast<size_t>(i) * 128,
+                          kStatBytes, &qd_full[s]);
                 issued = x + 1;
             }
             if (*abort_flag) {
@@ -593,11 +607,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 issue_s(0);
                 issue_dp(0);
             }
-            for (int x = 0; ok && x < n_q; ++x) {
+            for (int x = 0; ok && x < n_x; ++x) {
                 if (!(ok = mbar_wait(p1_full, x & 1, abort_flag))) break;
                 tc_fence_after();
                 issue_dv(x);
-                if (x + 1 < n_q) {
+                if (x + 1 < n_x) {
                     if (!(ok = mbar_wait(&qd_full[(x + 1) % NS], ((x + 1) / NS) & 1, abort_flag))) break;
                     tc_fence_after();
                     issue_s(x + 1);
@@ -605,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!(ok = mbar_wait(p2_full, x & 1, abort_flag))) break;
                 tc_fence_after();
                 issue_dk(x);
-                if (x + 1 < n_q) issue_dp(x + 1);
+                if (x + 1 < n_x) issue_dp(x + 1);
             }
             if (ok) mma_commit(acc_full);
             mma_commit(mma_done);
@@ -620,9 +634,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const float c2 = p.scale_log2;
         bool ok = true;
-        for (int x = 0; x < n_q; ++x) {
+        for (int x = 0; x < n_x; ++x) {
             const float4 *st = reinterpret_cast<const float4 *>(sRing + (x % NS) * STAGE + 2 * TILE);
-            const int qbase = (i0 + x) * 128;
+            const int qbase = (i0 + x % n_q) * 128;
             const int lo = p.causal ? key - qbase : 0;  // queries [0, lo) precede this key
             const int hi = p.S - qbase;                  // queries [hi, 128) are past the end
             const bool masked = __any_sync(0xffffffffu, lo > 0 || hi < 128);
@@ -704,8 +718,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(staged);
             if (threadIdx.x == 0 && mbar_wait(staged, 0, abort_flag)) {
                 for (int bx = 0; bx < C::kBoxes; ++bx) {
-                    tma_store_3d(&tm_dv, sK + bx * kBoxBytes, bx * kBoxCols, kt * 128, bh);
-                    tma_store_3d(&tm_dk, sV + bx * kBoxBytes, bx * kBoxCols, kt * 128, bh);
+                    tma_store_4d(&tm_dv, sK + bx * kBoxBytes, bx * kBoxCols, kt * 128, hkv, bb);
+                    tma_store_4d(&tm_dk, sV + bx * kBoxBytes, bx * kBoxCols, kt * 128, hkv, bb);
                 }
                 tma_store_commit();
                 tma_store_wait_read0();

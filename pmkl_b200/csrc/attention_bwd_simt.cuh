@@ -11,9 +11,12 @@
 //                            over the key tiles forms delta, a second forms dQ
 //                            (lane j scores key j; each lane accumulates dQ
 //                            columns lane, lane + 32, ...).  Writes delta.
-//   attn_bwd_simt_kv_kernel  32-row key tiles, 4 warps x 8 rows; lane j scores
-//                            query j of each 32-query tile, each lane
+//   attn_bwd_simt_kv_kernel  32-row key tiles of one K/V head, 4 warps x 8
+//                            rows; for every query head reading that K/V head
+//                            (grouped-query attention) and every 32-query
+//                            tile, lane j scores query j, each lane
 //                            accumulates dK/dV columns lane, lane + 32, ...
+// Tensors are addressed through the caller's strides (AttnBwdLayout).
 #pragma once
 
 #include "attention_simt.cuh"
@@ -31,7 +34,7 @@ __global__ void __launch_bounds__(kThreads)
     attn_bwd_simt_q_kernel(const T *__restrict__ dout, const T *__restrict__ q, const T *__restrict__ k,
                            const T *__restrict__ v, const T *__restrict__ m_in, const T *__restrict__ l_in,
                            T *__restrict__ dq, float *__restrict__ delta_out, int S, int D, int BH, int n_qt,
-                           int causal, float scale) {
+                           int causal, float scale, const AttnBwdLayout L) {
     extern __shared__ float smem_f[];
     constexpr int KS = DMAX + 1;
     constexpr int CPL = DMAX / 32;
@@ -45,16 +48,15 @@ __global__ void __launch_bounds__(kThreads)
     const int bid = blockIdx.x;
     const int qt = causal ? (n_qt - 1 - bid / BH) : (bid / BH);
     const int bh = bid % BH;
-    const size_t base = static_cast<size_t>(bh) * S * D;
+    const int bb = bh / L.H, hh = bh - bb * L.H, hkv = hh / L.kv_group;
     const int row0 = qt * 32;
 
     for (int idx = threadIdx.x; idx < 32 * DMAX; idx += kThreads) {
         const int r = idx / DMAX, d = idx % DMAX;
         const int row = row0 + r;
         const bool in = row < S && d < D;
-        const size_t g = base + static_cast<size_t>(row) * D + d;
-        Qs[idx] = in ? ld_f(q + g) : 0.f;
-        DOs[idx] = in ? ld_f(dout + g) : 0.f;
+        Qs[idx] = in ? ld_f(q + elem_off(L.q, bb, hh, row) + d) : 0.f;
+        DOs[idx] = in ? ld_f(dout + elem_off(L.dout, bb, hh, row) + d) : 0.f;
     }
     float mr[kRowsPerWarp], lr[kRowsPerWarp], part[kRowsPerWarp];
 #pragma unroll
@@ -93,9 +95,8 @@ __global__ void __launch_bounds__(kThreads)
             const int r = idx / DMAX, d = idx % DMAX;
             const int key = kb + r;
             const bool in = key < S && d < D;
-            const size_t g = base + static_cast<size_t>(key) * D + d;
-            Ks[r * KS + d] = in ? ld_f(k + g) : 0.f;
-            Vs[r * KS + d] = in ? ld_f(v + g) : 0.f;
+            Ks[r * KS + d] = in ? ld_f(k + elem_off(L.k, bb, hkv, key) + d) : 0.f;
+            Vs[r * KS + d] = in ? ld_f(v + elem_off(L.v, bb, hkv, key) + d) : 0.f;
         }
         __syncthreads();
     };
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = 0; i < kRowsPerWarp; ++i) {
         const int row = row0 + warp * kRowsPerWarp + i;
         if (row >= S) continue;
-        const size_t ob = base + static_cast<size_t>(row) * D;
+        const long long ob = elem_off(L.dq, bb, hh, row);
 #pragma unroll
         for (int t = 0; t < CPL; ++t) {
             const int d = lane + 32 * t;
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(kThreads)
     attn_bwd_simt_kv_kernel(const T *__restrict__ dout, const T *__restrict__ q, const T *__restrict__ k,
                             const T *__restrict__ v, const T *__restrict__ m_in, const T *__restrict__ l_in,
                             const float *__restrict__ delta_in, T *__restrict__ dk, T *__restrict__ dv, int S, int D,
-                            int BH, int causal, float scale) {
+                            int BHkv, int causal, float scale, const AttnBwdLayout L) {
     extern __shared__ float smem_f[];
     constexpr int QS = DMAX + 1;
     constexpr int CPL = DMAX / 32;
@@ -167,18 +168,18 @@ __global__ void __launch_bounds__(kThreads)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int kt = blockIdx.x / BH;  // causal: ascending = most query tiles first
-    const int bh = blockIdx.x % BH;
-    const size_t base = static_cast<size_t>(bh) * S * D;
+    const int kt = blockIdx.x / BHkv;  // causal: ascending = most query tiles first
+    const int bkv = blockIdx.x % BHkv;
+    const int Hkv = L.H / L.kv_group;
+    const int bb = bkv / Hkv, hkv = bkv - bb * Hkv;
     const int key0 = kt * 32;
 
     for (int idx = threadIdx.x; idx < 32 * DMAX; idx += kThreads) {
         const int r = idx / DMAX, d = idx % DMAX;
         const int key = key0 + r;
         const bool in = key < S && d < D;
-        const size_t g = base + static_cast<size_t>(key) * D + d;
-        Ks[idx] = in ? ld_f(k + g) : 0.f;
-        Vs[idx] = in ? ld_f(v + g) : 0.f;
+        Ks[idx] = in ? ld_f(k + elem_off(L.k, bb, hkv, key) + d) : 0.f;
+        Vs[idx] = in ? ld_f(v + elem_off(L.v, bb, hkv, key) + d) : 0.f;
     }
     float acc_k[kRowsPerWarp][CPL], acc_v[kRowsPerWarp][CPL];
 #pragma unroll
@@ -186,15 +187,21 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int t = 0; t < CPL; ++t) acc_k[i][t] = acc_v[i][t] = 0.f;
 
-    for (int qb = causal ? key0 : 0; qb < S; qb += 32) {
+    // Every query head of the group, each over its query tiles (the sum over
+    // the group is the gradient of the shared K/V head).
+    const int n_qb = (S - (causal ? key0 : 0) + 31) / 32;
+    for (int step = 0; step < L.kv_group * n_qb; ++step) {
+        const int g = step / n_qb;
+        const int qb = (causal ? key0 : 0) + (step - g * n_qb) * 32;
+        const int hh = hkv * L.kv_group + g;
+        const long long bh = static_cast<long long>(bb) * L.H + hh;
         __syncthreads();
         for (int idx = threadIdx.x; idx < 32 * DMAX; idx += kThreads) {
             const int r = idx / DMAX, d = idx % DMAX;
             const int qr = qb + r;
             const bool in = qr < S && d < D;
-            const size_t g = base + static_cast<size_t>(qr) * D + d;
-            Qs[r * QS + d] = in ? ld_f(q + g) : 0.f;
-            DOs[r * QS + d] = in ? ld_f(dout + g) : 0.f;
+            Qs[r * QS + d] = in ? ld_f(q + elem_off(L.q, bb, hh, qr) + d) : 0.f;
+            DOs[r * QS + d] = in ? ld_f(dout + elem_off(L.dout, bb, hh, qr) + d) : 0.f;
         }
         if (threadIdx.x < 32) {
             const int qr = qb + threadIdx.x;
@@ -241,13 +248,13 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = 0; i < kRowsPerWarp; ++i) {
         const int key = key0 + warp * kRowsPerWarp + i;
         if (key >= S) continue;
-        const size_t ob = base + static_cast<size_t>(key) * D;
+        const long long okk = elem_off(L.dk, bb, hkv, key), ovv = elem_off(L.dv, bb, hkv, key);
 #pragma unroll
         for (int t = 0; t < CPL; ++t) {
             const int d = lane + 32 * t;
             if (d < D) {
-                dk[ob + d] = Elem<T>::from_float(acc_k[i][t] * scale);
-                dv[ob + d] = Elem<T>::from_float(acc_v[i][t]);
+                dk[okk + d] = Elem<T>::from_float(acc_k[i][t] * scale);
+                dv[ovv + d] = Elem<T>::from_float(acc_v[i][t]);
             }
         }
     }

@@ -118,7 +118,8 @@ struct Params {
 // kernel's own; rows in [S, S_pad) get (0, 0).
 struct DeltaParams {
     int S_pad;
-    const void *dout;      // [BH][S][D], input dtype, contiguous
+    const void *dout;      // [B][H][S][D], input dtype, element strides do_s (batch, head, row)
+    long long do_s[3];
     const void *m_given;   // [BH][S]
     const void *l_given;
     float2 *rowstat;       // [BH][S_pad]
@@ -781,7 +782,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if constexpr (DELTA) {
                         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
                         const size_t ridx = static_cast<size_t>(w.bh) * p.S + row;
-                        const uint4 *drow = reinterpret_cast<const uint4 *>(static_cast<const T *>(dpar.dout) + ridx * D);
+                        const uint4 *drow = reinterpret_cast<const uint4 *>(
+                            static_cast<const T *>(dpar.dout) + bb * dpar.do_s[0] + hh * dpar.do_s[1] +
+                            static_cast<long long>(row) * dpar.do_s[2]);
                         float dot = 0.f;
 #pragma unroll
                         for (int cc = 0; cc < D / 32; ++cc) {

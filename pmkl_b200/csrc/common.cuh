@@ -57,6 +57,21 @@ struct AttnLayout {
     long long q[3], k[3], v[3], o[3];  // (batch, head, row)
 };
 
+// Element strides of the backward's tensors (batch, head, row) with the
+// head-size dimension contiguous.  q, dout, dq have H heads; k, v, dk, dv have
+// H / kv_group heads, query head h reading K/V head h / kv_group.  m, l and
+// the per-row terms are contiguous [batch * H][rows].
+struct AttnBwdLayout {
+    int H;
+    int kv_group;
+    long long dout[3], q[3], k[3], v[3], dq[3], dk[3], dv[3];
+};
+
+__host__ __device__ __forceinline__ long long elem_off(const long long (&st)[3], long long b, long long h,
+                                                        long long row) {
+    return b * st[0] + h * st[1] + row * st[2];
+}
+
 // Stores one fp32 value as out_dtype.
 __device__ __forceinline__ void store_as(void *base, size_t idx, int out_dtype, float v) {
     if (out_dtype == PMKL_DTYPE_F32)

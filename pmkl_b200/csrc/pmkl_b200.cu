@@ -221,6 +221,7 @@ bool pp_launchable() {
 // row statistics (b, delta) from dO and the caller's m~, l~.
 struct DeltaArgs {
     const void *dout;
+    long long do_s[3];  // element strides of dout (batch, head, row)
     const void *m_given;
     const void *l_given;
     float2 *rowstat;
@@ -284,7 +285,14 @@ int launch_pp(const void *q, const void *k, const void *v, void *o, void *m, voi
     p.m_out = m;
     p.l_out = l;
     pp::DeltaParams dp{};
-    if (delta) dp = pp::DeltaParams{delta->S_pad, delta->dout, delta->m_given, delta->l_given, delta->rowstat};
+    if (delta) {
+        dp.S_pad = delta->S_pad;
+        dp.dout = delta->dout;
+        for (int i = 0; i < 3; ++i) dp.do_s[i] = delta->do_s[i];
+        dp.m_given = delta->m_given;
+        dp.l_given = delta->l_given;
+        dp.rowstat = delta->rowstat;
+    }
     const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
     p.n_rounds = static_cast<int>((units + grid - 1) / grid);
     kernel<<<grid, pp::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, p, dp);
@@ -446,11 +454,14 @@ BwdLayout bwd_layout_tc(long long BH, int S, int D) {
 // Workspace of the CUDA-core backward: delta per row.
 size_t bwd_ws_simt(long long BH, int S) { return align256(static_cast<size_t>(BH) * S * 4); }
 
-bool bwd_tc_applies(const void *const (&ptrs)[9], int D, int dtype) {
+bool bwd_tc_applies(const void *const (&ptrs)[9], int D, int dtype, const AttnBwdLayout &lay) {
     if (dtype != PMKL_DTYPE_F16 && dtype != PMKL_DTYPE_BF16) return false;
     if (D != 64 && D != 128) return false;
     for (const void *p : ptrs)
         if (!aligned16(p)) return false;
+    // TMA: every stride a multiple of 16 bytes.
+    for (const auto *st : {&lay.dout, &lay.q, &lay.k, &lay.v, &lay.dq, &lay.dk, &lay.dv})
+        if (!strides_ok(*st, 8)) return false;
     return true;
 }
 
@@ -469,69 +480,100 @@ int launch_bwd_rowstat(const void *dout, const float *o32, const float *m32, con
 
 template <int D, bool BF16>
 int launch_bwd_tc(const void *dout, const void *q, const void *k, const void *v, void *dq, void *dk, void *dv, int S,
-                  int BH, int causal, float scale, int dtype, const float2 *rowstat, int S_pad, cudaStream_t stream) {
+                  int BH, int causal, float scale, int dtype, const float2 *rowstat, int S_pad,
+                  const AttnBwdLayout &lay, cudaStream_t stream) {
     static std::once_flag once_q[kMaxDevices], once_kv[kMaxDevices];
     auto kq = bwd::attn_bwd_dq_kernel<D, BF16>;
     auto kkv = bwd::attn_bwd_dkv_kernel<D, BF16>;
     constexpr int smem_q = bwd::CfgQ<D>::kSmemBytes;
     constexpr int smem_kv = bwd::CfgKV<D>::kSmemBytes;
     if (!ensure_smem(kq, smem_q, once_q) || !ensure_smem(kkv, smem_kv, once_kv)) return PMKL_ERR_LAUNCH;
+    const int B = BH / lay.H, Hkv = lay.H / lay.kv_group;
     CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
-    if (!make_tile_map(&tq, q, dtype, D, S, BH) || !make_tile_map(&tk, k, dtype, D, S, BH) ||
-        !make_tile_map(&tv, v, dtype, D, S, BH) || !make_tile_map(&tdo, dout, dtype, D, S, BH) ||
-        !make_tile_map(&tdq, dq, dtype, D, S, BH) || !make_tile_map(&tdk, dk, dtype, D, S, BH) ||
-        !make_tile_map(&tdv, dv, dtype, D, S, BH))
+    if (!make_tile_map_4d(&tq, q, dtype, D, S, lay.H, B, lay.q) ||
+        !make_tile_map_4d(&tk, k, dtype, D, S, Hkv, B, lay.k) ||
+        !make_tile_map_4d(&tv, v, dtype, D, S, Hkv, B, lay.v) ||
+        !make_tile_map_4d(&tdo, dout, dtype, D, S, lay.H, B, lay.dout) ||
+        !make_tile_map_4d(&tdq, dq, dtype, D, S, lay.H, B, lay.dq) ||
+        !make_tile_map_4d(&tdk, dk, dtype, D, S, Hkv, B, lay.dk) ||
+        !make_tile_map_4d(&tdv, dv, dtype, D, S, Hkv, B, lay.dv))
         return PMKL_ERR_LAUNCH;
     bwd::Params p;
     p.S = S;
     p.S_pad = S_pad;
     p.BH = BH;
+    p.H = lay.H;
+    p.kv_group = lay.kv_group;
+    p.BHkv = B * Hkv;
     p.n_qt = (S + 127) / 128;
     p.causal = causal;
     p.scale = scale;
     p.scale_log2 = scale * bwd::kLog2e;
     p.rowstat = rowstat;
-    const long long blocks = static_cast<long long>(p.n_qt) * BH;
-    if (blocks > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
-    kq<<<static_cast<unsigned>(blocks), bwd::kThreads, smem_q, stream>>>(tq, tk, tv, tdo, tdq, p);
+    const long long blocks_q = static_cast<long long>(p.n_qt) * BH;
+    const long long blocks_kv = static_cast<long long>(p.n_qt) * p.BHkv;
+    if (blocks_q > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
+    kq<<<static_cast<unsigned>(blocks_q), bwd::kThreads, smem_q, stream>>>(tq, tk, tv, tdo, tdq, p);
     const int rc = launch_status();
     if (rc != PMKL_OK) return rc;
-    kkv<<<static_cast<unsigned>(blocks), bwd::kThreads, smem_kv, stream>>>(tq, tk, tv, tdo, tdk, tdv, p);
+    kkv<<<static_cast<unsigned>(blocks_kv), bwd::kThreads, smem_kv, stream>>>(tq, tk, tv, tdo, tdk, tdv, p);
     return launch_status();
 }
 
 template <typename T, int DMAX>
 int launch_bwd_simt_t(const void *dout, const void *q, const void *k, const void *v, const void *m, const void *l,
                       void *dq, void *dk, void *dv, float *delta, int S, int D, int BH, int causal, float scale,
-                      cudaStream_t stream) {
+                      const AttnBwdLayout &lay, cudaStream_t stream) {
     static std::once_flag once_q[kMaxDevices], once_kv[kMaxDevices];
     auto kq = simt::attn_bwd_simt_q_kernel<T, DMAX>;
     auto kkv = simt::attn_bwd_simt_kv_kernel<T, DMAX>;
     constexpr int smem = simt::bwd_smem_bytes<DMAX>();
     if (!ensure_smem(kq, smem, once_q) || !ensure_smem(kkv, smem, once_kv)) return PMKL_ERR_LAUNCH;
     const int n_t = (S + 31) / 32;
+    const int BHkv = BH / lay.kv_group;
     const long long blocks = static_cast<long long>(n_t) * BH;
+    const long long blocks_kv = static_cast<long long>(n_t) * BHkv;
     if (blocks > 0x7FFFFFFFLL) return PMKL_ERR_INVALID_SHAPE;
     const T *tdo = static_cast<const T *>(dout), *tq = static_cast<const T *>(q), *tk = static_cast<const T *>(k),
             *tv = static_cast<const T *>(v), *tm = static_cast<const T *>(m), *tl = static_cast<const T *>(l);
     kq<<<static_cast<unsigned>(blocks), simt::kThreads, smem, stream>>>(tdo, tq, tk, tv, tm, tl, static_cast<T *>(dq),
-                                                                        delta, S, D, BH, n_t, causal, scale);
+                                                                        delta, S, D, BH, n_t, causal, scale, lay);
     const int rc = launch_status();
     if (rc != PMKL_OK) return rc;
-    kkv<<<static_cast<unsigned>(blocks), simt::kThreads, smem, stream>>>(
-        tdo, tq, tk, tv, tm, tl, delta, static_cast<T *>(dk), static_cast<T *>(dv), S, D, BH, causal, scale);
+    kkv<<<static_cast<unsigned>(blocks_kv), simt::kThreads, smem, stream>>>(
+        tdo, tq, tk, tv, tm, tl, delta, static_cast<T *>(dk), static_cast<T *>(dv), S, D, BHkv, causal, scale, lay);
     return launch_status();
 }
 
 template <typename T>
 int launch_bwd_simt(const void *dout, const void *q, const void *k, const void *v, const void *m, const void *l,
                     void *dq, void *dk, void *dv, float *delta, int S, int D, int BH, int causal, float scale,
-                    cudaStream_t stream) {
-    if (D <= 32) return launch_bwd_simt_t<T, 32>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
-    if (D <= 64) return launch_bwd_simt_t<T, 64>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
+                    const AttnBwdLayout &lay, cudaStream_t stream) {
+    if (D <= 32)
+        return launch_bwd_simt_t<T, 32>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, lay, stream);
+    if (D <= 64)
+        return launch_bwd_simt_t<T, 64>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, lay, stream);
     if (D <= 128)
-        return launch_bwd_simt_t<T, 128>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
-    return launch_bwd_simt_t<T, 256>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, stream);
+        return launch_bwd_simt_t<T, 128>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, lay, stream);
+    return launch_bwd_simt_t<T, 256>(dout, q, k, v, m, l, dq, dk, dv, delta, S, D, BH, causal, scale, lay, stream);
+}
+
+AttnBwdLayout contiguous_bwd_layout(int H, int S, int D) {
+    AttnBwdLayout L;
+    L.H = H;
+    L.kv_group = 1;
+    const long long s3[3] = {static_cast<long long>(H) * S * D, static_cast<long long>(S) * D, D};
+    for (int i = 0; i < 3; ++i) L.dout[i] = L.q[i] = L.k[i] = L.v[i] = L.dq[i] = L.dk[i] = L.dv[i] = s3[i];
+    return L;
+}
+
+bool bwd_layout_contiguous(const AttnBwdLayout &L, int S, int D) {
+    const AttnBwdLayout c = contiguous_bwd_layout(L.H, S, D);
+    for (int i = 0; i < 3; ++i)
+        if (L.dout[i] != c.dout[i] || L.q[i] != c.q[i] || L.k[i] != c.k[i] || L.v[i] != c.v[i] ||
+            L.dq[i] != c.dq[i] || L.dk[i] != c.dk[i] || L.dv[i] != c.dv[i])
+            return false;
+    return L.kv_group == 1;
 }
 
 // Scratch of pmkl_causal_attention_bwd_static: static device memory of this
@@ -575,7 +617,7 @@ size_t bwd_workspace_size(long long BH, int S, int D, int dtype, int kernel) {
 int attention_bwd_impl(const void *dout, const void *q, const void *k, const void *v, const void *m, const void *l,
                        void *dq, void *dk, void *dv, int batch, int heads, int seq, int hidden, int dtype,
                        int is_causal, float scale, void *workspace, size_t workspace_bytes, int kernel,
-                       void *stream_) {
+                       void *stream_, const AttnBwdLayout *layout = nullptr) {
     if (batch < 0 || heads < 0 || seq < 0 || hidden < 0) return PMKL_ERR_INVALID_SHAPE;
     if (!dtype_valid(dtype)) return PMKL_ERR_INVALID_DTYPE;
     if (kernel != PMKL_ATTN_AUTO && kernel != PMKL_ATTN_SIMT && kernel != PMKL_ATTN_TCGEN05 &&
@@ -593,9 +635,14 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     const int causal = is_causal ? 1 : 0;
     const int bh = static_cast<int>(BH);
+    const AttnBwdLayout lay = layout ? *layout : contiguous_bwd_layout(heads, seq, hidden);
+    const bool contiguous = bwd_layout_contiguous(lay, seq, hidden);
     const void *const ptrs[9] = {dout, q, k, v, m, l, dq, dk, dv};
-    const bool tc_ok = bwd_tc_applies(ptrs, hidden, dtype);
+    const bool tc_ok = bwd_tc_applies(ptrs, hidden, dtype, lay);
     if ((kernel == PMKL_ATTN_TCGEN05 || kernel == PMKL_ATTN_TCGEN05_SIMPLE) && !tc_ok) return PMKL_ERR_UNSUPPORTED;
+    // The long route's forward and row-statistics kernel read contiguous,
+    // equal-head tensors only.
+    if (kernel == PMKL_ATTN_TCGEN05_SIMPLE && !contiguous) return PMKL_ERR_UNSUPPORTED;
     const bool bf = dtype == PMKL_DTYPE_BF16;
     // delta = sum_j p dP comes from this library's forward through dO . O: the
     // persistent kernel forms it in its epilogue (O never leaves tensor
@@ -610,24 +657,33 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
     // workspace holds it and the CUDA-core route otherwise, so that the size
     // pmkl_causal_attention_bwd_workspace_size reports always suffices.
     const bool tc_route = tc_ok && kernel != PMKL_ATTN_SIMT &&
-                          (fused || kernel != PMKL_ATTN_AUTO || workspace_bytes >= L.total);
+                          (fused || (contiguous && (kernel != PMKL_ATTN_AUTO || workspace_bytes >= L.total)));
+    if (kernel == PMKL_ATTN_TCGEN05 && !tc_route) return PMKL_ERR_UNSUPPORTED;
     if (tc_route) {
         if (workspace_bytes < (fused ? L.fused_total : L.total)) return PMKL_ERR_WORKSPACE;
         uint8_t *ws = static_cast<uint8_t *>(workspace);
         float2 *rowstat = reinterpret_cast<float2 *>(ws + L.rowstat);
         int rc;
         if (fused) {
-            const DeltaArgs da{dout, m, l, rowstat, L.S_pad};
-            const AttnLayout lay = contiguous_layout(heads, seq, hidden);
+            const DeltaArgs da{dout, {lay.dout[0], lay.dout[1], lay.dout[2]}, m, l, rowstat, L.S_pad};
+            // The forward reads q, k, v through their strides; it writes no O.
+            AttnLayout fl;
+            fl.H = lay.H;
+            fl.kv_group = lay.kv_group;
+            for (int i = 0; i < 3; ++i) {
+                fl.q[i] = fl.o[i] = lay.q[i];
+                fl.k[i] = lay.k[i];
+                fl.v[i] = lay.v[i];
+            }
             rc = hidden == 64
                      ? (bf ? launch_pp<64, true>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal, sc,
-                                                 dtype, dtype, lay, stream, &da)
+                                                 dtype, dtype, fl, stream, &da)
                            : launch_pp<64, false>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal, sc,
-                                                  dtype, dtype, lay, stream, &da))
+                                                  dtype, dtype, fl, stream, &da))
                      : (bf ? launch_pp<128, true>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal, sc,
-                                                  dtype, dtype, lay, stream, &da)
+                                                  dtype, dtype, fl, stream, &da)
                            : launch_pp<128, false>(q, k, v, const_cast<void *>(q), nullptr, nullptr, seq, bh, causal,
-                                                   sc, dtype, dtype, lay, stream, &da));
+                                                   sc, dtype, dtype, fl, stream, &da));
         } else {
             float *o32 = reinterpret_cast<float *>(ws + L.o);
             float *m32 = reinterpret_cast<float *>(ws + L.m);
@@ -643,21 +699,23 @@ int attention_bwd_impl(const void *dout, const void *q, const void *k, const voi
         if (rc != PMKL_OK) return rc;
         if (dtype == PMKL_DTYPE_BF16)
             return hidden == 64 ? launch_bwd_tc<64, true>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype,
-                                                          rowstat, L.S_pad, stream)
+                                                          rowstat, L.S_pad, lay, stream)
                                 : launch_bwd_tc<128, true>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype,
-                                                           rowstat, L.S_pad, stream);
+                                                           rowstat, L.S_pad, lay, stream);
         return hidden == 64 ? launch_bwd_tc<64, false>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype, rowstat,
-                                                       L.S_pad, stream)
+                                                       L.S_pad, lay, stream)
                             : launch_bwd_tc<128, false>(dout, q, k, v, dq, dk, dv, seq, bh, causal, sc, dtype, rowstat,
-                                                        L.S_pad, stream);
+                                                        L.S_pad, lay, stream);
     }
     if (workspace_bytes < bwd_ws_simt(BH, seq)) return PMKL_ERR_WORKSPACE;
     float *delta = static_cast<float *>(workspace);
     if (dtype == PMKL_DTYPE_F32)
-        return launch_bwd_simt<float>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, stream);
+        return launch_bwd_simt<float>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, lay, stream);
     if (dtype == PMKL_DTYPE_F16)
-        return launch_bwd_simt<__half>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, stream);
-    return launch_bwd_simt<__nv_bfloat16>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, stream);
+        return launch_bwd_simt<__half>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, lay,
+                                       stream);
+    return launch_bwd_simt<__nv_bfloat16>(dout, q, k, v, m, l, dq, dk, dv, delta, seq, hidden, bh, causal, sc, lay,
+                                          stream);
 }
 
 // ------------------------------------------------------------------ softmax launchers
@@ -754,6 +812,38 @@ int pmkl_causal_attention_bwd_ex(const void *dout, const void *q, const void *k,
                                  size_t workspace_bytes, int kernel, void *stream) {
     return attention_bwd_impl(dout, q, k, v, m, l, dq, dk, dv, batch, heads, seq, hidden, dtype, is_causal, scale,
                               workspace, workspace_bytes, kernel, stream);
+}
+
+int pmkl_causal_attention_bwd_strided(const void *dout, const void *q, const void *k, const void *v, const void *m,
+                                      const void *l, void *dq, void *dk, void *dv, int batch, int heads, int kv_heads,
+                                      int seq, int hidden, const int64_t *dout_strides, const int64_t *q_strides,
+                                      const int64_t *k_strides, const int64_t *v_strides, const int64_t *dq_strides,
+                                      const int64_t *dk_strides, const int64_t *dv_strides, int dtype, int is_causal,
+                                      float scale, void *workspace, size_t workspace_bytes, int kernel,
+                                      void *stream) {
+    if (batch < 0 || heads < 0 || seq < 0 || hidden < 0 || kv_heads < 0) return PMKL_ERR_INVALID_SHAPE;
+    if (heads > 0 && (kv_heads == 0 || heads % kv_heads != 0)) return PMKL_ERR_INVALID_SHAPE;
+    AttnBwdLayout lay = contiguous_bwd_layout(heads > 0 ? heads : 1, seq, hidden);
+    lay.kv_group = (heads > 0 && kv_heads > 0) ? heads / kv_heads : 1;
+    const long long Hkv = kv_heads > 0 ? kv_heads : 1;
+    const long long kv_contig[3] = {Hkv * seq * hidden, static_cast<long long>(seq) * hidden, hidden};
+    const int64_t *given[7] = {dout_strides, q_strides, k_strides, v_strides, dq_strides, dk_strides, dv_strides};
+    long long *dst[7] = {lay.dout, lay.q, lay.k, lay.v, lay.dq, lay.dk, lay.dv};
+    for (int t = 0; t < 7; ++t) {
+        const bool kv_shaped = t == 2 || t == 3 || t == 5 || t == 6;
+        const long long extent[3] = {batch, kv_shaped ? Hkv : heads, seq};
+        for (int i = 0; i < 3; ++i) {
+            if (given[t]) {
+                if (given[t][i] < 0) return PMKL_ERR_INVALID_SHAPE;
+                // A dimension of extent 1 is never stepped: its stride does not matter.
+                dst[t][i] = extent[i] == 1 ? 0 : given[t][i];
+            } else if (kv_shaped) {
+                dst[t][i] = kv_contig[i];
+            }
+        }
+    }
+    return attention_bwd_impl(dout, q, k, v, m, l, dq, dk, dv, batch, heads, seq, hidden, dtype, is_causal, scale,
+                              workspace, workspace_bytes, kernel, stream, &lay);
 }
 
 int pmkl_causal_attention_bwd_static(const void *dout, const void *q, const void *k, const void *v, const void *m,

@@ -6,6 +6,8 @@
 // through the C ABI of libpmkl_b200 (include/pmkl_b200.h) on the current
 // CUDA stream instead of the reference's single-threaded host loops.  There is
 // no CPU path: CPU tensors are rejected.
+#include <array>
+
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/extension.h>
@@ -106,12 +108,10 @@ namespace {
 std::tuple<at::Tensor, at::Tensor, at::Tensor> backward_impl(const at::Tensor &dout, const at::Tensor &q,
                                                              const at::Tensor &k, const at::Tensor &v,
                                                              const at::Tensor &out_m, const at::Tensor &out_l,
-                                                             bool is_causal, int64_t kernel, double scale) {
+                                                             bool is_causal, int64_t kernel, double scale,
+                                                             bool allow_kv_heads) {
     // fused_self_attention.cpp:178-180
-    TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "Input tensor shapes must match");
-    TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "Input tensor must be contiguous");
-    TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(), "Input tensor shapes must match");
-    check_inputs(q, k, v);
+    check_inputs(q, k, v, allow_kv_heads);
     TORCH_CHECK(dout.sizes() == q.sizes(), "fused_self_attention_bw: grad_output must have q's shape");
     const std::vector<int64_t> stat_shape = {q.size(0), q.size(1), q.size(2)};
     TORCH_CHECK(out_m.sizes() == stat_shape && out_l.sizes() == stat_shape,
@@ -125,18 +125,31 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> backward_impl(const at::Tensor &d
     const c10::cuda::CUDAGuard guard(q.device());
     const int B = static_cast<int>(q.size(0)), H = static_cast<int>(q.size(1));
     const int S = static_cast<int>(q.size(2)), D = static_cast<int>(q.size(3));
-    const at::Tensor dc = dout.contiguous(), mc = out_m.contiguous(), lc = out_l.contiguous();
-    // Every element is written, so empty (not zeros, :186-188) gives the same result.
-    at::Tensor dq = at::empty_like(q), dk = at::empty_like(k), dv = at::empty_like(v);
+    const int Hkv = static_cast<int>(k.size(1));
+    // The reference makes its inputs contiguous (fused_self_attention.cpp:179);
+    // here views are read in place through their strides and copied only when
+    // the hidden dimension itself is strided.
+    const auto rows_ok = [](const at::Tensor &t) { return t.size(3) <= 1 || t.stride(3) == 1; };
+    const at::Tensor dc = rows_ok(dout) ? dout : dout.contiguous();
+    const at::Tensor qc = rows_ok(q) ? q : q.contiguous();
+    const at::Tensor kc = rows_ok(k) ? k : k.contiguous();
+    const at::Tensor vc = rows_ok(v) ? v : v.contiguous();
+    const at::Tensor mc = out_m.contiguous(), lc = out_l.contiguous();
+    // Every element is written, so empty (not zeros, :186-188) gives the same
+    // result.  The gradients take their inputs' layout (dense views keep their
+    // strides) and are written in place through them.
+    at::Tensor dq = at::empty_like(qc), dk = at::empty_like(kc), dv = at::empty_like(vc);
     const int dt = pmkl_dtype_of(v.scalar_type());
     const size_t ws_bytes = pmkl_causal_attention_bwd_workspace_size_ex(B, H, S, D, dt, static_cast<int>(kernel));
     at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes > 0 ? ws_bytes : 1)}, q.options().dtype(at::kByte));
+    const auto st = [](const at::Tensor &t) { return std::array<int64_t, 3>{t.stride(0), t.stride(1), t.stride(2)}; };
+    const auto sdo = st(dc), sq = st(qc), sk = st(kc), sv = st(vc), sdq = st(dq), sdk = st(dk), sdv = st(dv);
     cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
-    const int rc = pmkl_causal_attention_bwd_ex(dc.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                                mc.data_ptr(), lc.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                                dv.data_ptr(), B, H, S, D, dt, is_causal ? 1 : 0,
-                                                static_cast<float>(scale), ws.data_ptr(), ws_bytes,
-                                                static_cast<int>(kernel), stream);
+    const int rc = pmkl_causal_attention_bwd_strided(
+        dc.data_ptr(), qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), mc.data_ptr(), lc.data_ptr(), dq.data_ptr(),
+        dk.data_ptr(), dv.data_ptr(), B, H, Hkv, S, D, sdo.data(), sq.data(), sk.data(), sv.data(), sdq.data(),
+        sdk.data(), sdv.data(), dt, is_causal ? 1 : 0, static_cast<float>(scale), ws.data_ptr(), ws_bytes,
+        static_cast<int>(kernel), stream);
     TORCH_CHECK(rc == PMKL_OK, "pmkl_causal_attention_bwd failed: ", pmkl_status_string(rc));
     return std::make_tuple(dq, dk, dv);
 }
@@ -148,14 +161,17 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> fused_self_attention_bw(const at:
                                                                        const at::Tensor &k, const at::Tensor &v,
                                                                        const at::Tensor &out_m,
                                                                        const at::Tensor &out_l, bool is_causal) {
-    return backward_impl(dout, q, k, v, out_m, out_l, is_causal, PMKL_ATTN_AUTO, 0.0);
+    return backward_impl(dout, q, k, v, out_m, out_l, is_causal, PMKL_ATTN_AUTO, 0.0, false);
 }
 
-// Extra entry (no reference counterpart): explicit kernel choice and scale.
+// Extra entry (no reference counterpart): explicit kernel choice and scale,
+// and k, v with fewer heads than q (grouped-query: dk, dv are the sums over
+// the query heads that read each K/V head) -- the backward of
+// fused_self_attention_fw_ex.
 std::tuple<at::Tensor, at::Tensor, at::Tensor> fused_self_attention_bw_ex(
     const at::Tensor &dout, const at::Tensor &q, const at::Tensor &k, const at::Tensor &v, const at::Tensor &out_m,
     const at::Tensor &out_l, bool is_causal, int64_t kernel, double scale) {
-    return backward_impl(dout, q, k, v, out_m, out_l, is_causal, kernel, scale);
+    return backward_impl(dout, q, k, v, out_m, out_l, is_causal, kernel, scale, true);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

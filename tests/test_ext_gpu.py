@@ -131,14 +131,29 @@ def test_bw_matches_capi_bitwise():
 def test_bw_errors():
     q = torch.randn(1, 2, 8, 64, device="cuda")
     m = torch.zeros(1, 2, 8, device="cuda")
-    with pytest.raises(RuntimeError, match="contiguous"):
-        pmkl_pytorch_ext.fused_self_attention_bw(q, q.transpose(2, 3).contiguous().transpose(2, 3), q, q, m, m, True)
+    with pytest.raises(RuntimeError, match="shapes must match"):
+        pmkl_pytorch_ext.fused_self_attention_bw(q, q, q[:, :1], q[:, :1], m, m, True)  # reference API: equal heads
     with pytest.raises(RuntimeError, match="v's dtype"):
         pmkl_pytorch_ext.fused_self_attention_bw(q, q, q, q, m.half(), m, True)
     with pytest.raises(RuntimeError, match="batch, heads, seq"):
         pmkl_pytorch_ext.fused_self_attention_bw(q, q, q, q, m[:, :1], m, True)
     with pytest.raises(RuntimeError, match="CUDA"):
         pmkl_pytorch_ext.fused_self_attention_bw(q, q.cpu(), q.cpu(), q.cpu(), m, m, True)
+
+
+def test_bw_strided_hidden_dimension_is_copied():
+    """A strided hidden dimension (here a transposed last pair of axes) is
+    made contiguous before the call, as the reference makes every input
+    contiguous (fused_self_attention.cpp:179); the result matches."""
+    q = torch.randn(1, 2, 64, 64, device="cuda")
+    qt = q.transpose(2, 3).contiguous().transpose(2, 3)
+    assert qt.stride(3) != 1
+    m = torch.zeros(1, 2, 64, device="cuda")
+    l = torch.ones(1, 2, 64, device="cuda")
+    a = pmkl_pytorch_ext.fused_self_attention_bw(q, qt, q, q, m, l, True)
+    b = pmkl_pytorch_ext.fused_self_attention_bw(q, q, q, q, m, l, True)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
 
 
 def test_empty_inputs():

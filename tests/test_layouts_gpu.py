@@ -162,3 +162,172 @@ def test_autograd_through_views():
     assert torch.equal(out, out2)
     for a, b in ((q.grad, q2.grad), (k.grad, k2.grad), (v.grad, v2.grad)):
         assert torch.equal(a, b)
+
+
+# ------------------------------------------------------------------ backward: strided and grouped-query
+def stats(q, k, v, causal):
+    """m, l of this library's forward in the inputs' dtype (what autograd saves)."""
+    _, m, l = run_strided(q, k, v, causal)
+    return m, l
+
+
+def run_bwd_strided(dout, q, k, v, m, l, causal, kernel=0, outs=None):
+    dq, dk, dv = outs if outs is not None else (torch.empty(q.shape, dtype=q.dtype, device="cuda"),
+                                                torch.empty(k.shape, dtype=k.dtype, device="cuda"),
+                                                torch.empty(v.shape, dtype=v.dtype, device="cuda"))
+    pmkl_b200.attention_bwd_strided(dout, q, k, v, m, l, dq, dk, dv, causal, kernel=kernel)
+    torch.cuda.synchronize()
+    return dq, dk, dv
+
+
+def run_bwd_contiguous(dout, q, k, v, m, l, causal, kernel=0):
+    t = [x.contiguous() for x in (dout, q, k, v, m, l)]
+    out = [torch.empty_like(t[1]) for _ in range(3)]
+    pmkl_b200.attention_bwd(*t, *out, causal, kernel=kernel)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("kernel,dtype,D", [(TC, torch.bfloat16, 128), (TC, torch.float16, 64),
+                                            (SIMT, torch.float32, 64), (SIMT, torch.bfloat16, 96)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_bwd_bshd_views_match_contiguous(kernel, dtype, D, causal):
+    """The backward reads [B, S, H, D] views in place: bit for bit the same
+    gradients as the same kernel on contiguous copies."""
+    B, H, S = 2, 4, 300
+    q, k, v, dout = (bshd_view(B, H, S, D, dtype, s) for s in (31, 32, 33, 34))
+    m, l = stats(q, k, v, causal)
+    got = run_bwd_strided(dout, q, k, v, m, l, causal, kernel=kernel)
+    ref = run_bwd_contiguous(dout, q, k, v, m, l, causal, kernel=kernel)
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("kernel", [TC, SIMT])
+def test_bwd_strided_gradients_written_in_place(kernel):
+    B, H, S, D = 2, 3, 257, 128
+    q, k, v, dout = (randn((B, H, S, D), torch.bfloat16, s) for s in (35, 36, 37, 38))
+    m, l = stats(q, k, v, True)
+    bufs = [torch.empty(B, S, H, D, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    run_bwd_strided(dout, q, k, v, m, l, True, kernel=kernel, outs=[t.transpose(1, 2) for t in bufs])
+    ref = run_bwd_contiguous(dout, q, k, v, m, l, True, kernel=kernel)
+    for a, b in zip(bufs, ref):
+        assert torch.equal(a.transpose(1, 2), b)
+
+
+def group_oracle(dout, q, k, v, m, l, causal, g):
+    """Oracle gradients of grouped-query attention: the ordinary backward on
+    K/V repeated over each group, dk and dv summed over the group's heads."""
+    rk, rv = (np32(t).repeat(g, axis=1) for t in (k, v))
+    dq, dk, dv = oracle.attention_bwd(np32(dout), np32(q), rk, rv, np32(m), np32(l), causal)
+    B, H, S, D = dq.shape
+    return dq, dk.reshape(B, H // g, g, S, D).sum(2), dv.reshape(B, H // g, g, S, D).sum(2)
+
+
+def assert_grads_close(got, ref, dtype, what):
+    from test_attention_bwd_gpu import assert_grad_close
+    for a, r, n in zip(got, ref, ("dq", "dk", "dv")):
+        assert_grad_close(np32(a), r, dtype, f"{what} {n}")
+
+
+@pytest.mark.parametrize("kernel,dtype,D", [(TC, torch.bfloat16, 128), (TC, torch.float16, 64),
+                                            (SIMT, torch.float32, 64), (SIMT, torch.bfloat16, 96)])
+@pytest.mark.parametrize("kv_heads", [1, 2])
+def test_bwd_grouped_query_against_oracle(kv_heads, kernel, dtype, D):
+    """Grouped-query backward: dk, dv of each K/V head are the sums over its
+    query heads (formed in fp32 inside the kernel); checked against the
+    oracle on repeated K/V with the backward tests' tolerances."""
+    B, H, S = 1, 4, 200
+    g = H // kv_heads
+    q, dout = (randn((B, H, S, D), dtype, s) for s in (40, 41))
+    k, v = (bshd_view(B, kv_heads, S, D, dtype, s) for s in (42, 43))
+    m, l = stats(q, k, v, True)
+    got = run_bwd_strided(dout, q, k, v, m, l, True, kernel=kernel)
+    ref = group_oracle(dout, q, k, v, m, l, True, g)
+    assert_grads_close(got, ref, dtype, f"gqa kv_heads={kv_heads}")
+    # dq reads the shared K/V exactly as the repeated form does: bit for bit.
+    rep = run_bwd_contiguous(dout, q, k.repeat_interleave(g, dim=1), v.repeat_interleave(g, dim=1), m, l, True,
+                             kernel=kernel)
+    assert torch.equal(got[0], rep[0])
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_bwd_grouped_query_long_sequence(D):
+    """Several query tiles per head and a ring that wraps across the group's
+    heads in the dK/dV kernel (S = 1024, 4 query heads per K/V head)."""
+    B, H, Hkv, S = 1, 8, 2, 1024
+    q, dout = (randn((B, H, S, D), torch.bfloat16, s) for s in (44, 45))
+    k, v = (randn((B, Hkv, S, D), torch.bfloat16, s) for s in (46, 47))
+    m, l = stats(q, k, v, True)
+    got = run_bwd_strided(dout, q, k, v, m, l, True, kernel=TC)
+    ref = group_oracle(dout, q, k, v, m, l, True, H // Hkv)
+    assert_grads_close(got, ref, torch.bfloat16, f"gqa S1024 D{D}")
+
+
+def test_bwd_strided_errors():
+    import ctypes
+    L = pmkl_b200.capi()
+    f = 0x10000
+    s = (ctypes.c_int64 * 3)(64 * 8 * 128, 128, 8 * 128)
+    neg = (ctypes.c_int64 * 3)(1, -1, 1)
+
+    def call(heads=8, kv=2, st=s, kernel=0):
+        return L.pmkl_causal_attention_bwd_strided(*([f] * 9), 1, heads, kv, 64, 128, st, st, st, st, st, st, st, 2,
+                                                   1, 0.0, f, 1 << 20, kernel, None)
+
+    assert call(kv=3) == -1  # kv_heads must divide heads
+    assert call(kv=0) == -1
+    assert call(st=neg) == -1
+    q, dout = (randn((1, 4, 64, 64), torch.bfloat16, s) for s in (48, 49))
+    k, v = (randn((1, 2, 64, 64), torch.bfloat16, s) for s in (50, 51))
+    m, l = stats(q, k, v, True)
+    with pytest.raises(pmkl_b200.PmklError, match="UNSUPPORTED"):
+        run_bwd_strided(dout, q, k, v, m, l, True, kernel=3)  # the long route takes equal heads only
+
+
+def test_bwd_unaligned_row_stride_takes_cuda_core_path():
+    B, H, S, D = 1, 2, 130, 64
+    base = randn((B, H, S, D + 1), torch.bfloat16, 52)
+    q = base[..., :D]
+    k, v, dout = (randn((B, H, S, D), torch.bfloat16, s) for s in (53, 54, 55))
+    m, l = stats(q, k, v, True)
+    got = run_bwd_strided(dout, q, k, v, m, l, True)
+    ref = run_bwd_contiguous(dout, q, k, v, m, l, True, kernel=SIMT)
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    with pytest.raises(pmkl_b200.PmklError, match="UNSUPPORTED"):
+        run_bwd_strided(dout, q, k, v, m, l, True, kernel=TC)
+
+
+def test_extension_backward_reads_views_without_copies():
+    B, H, S, D = 2, 16, 1024, 128
+    q, k, v, dout = (bshd_view(B, H, S, D, torch.bfloat16, s) for s in (56, 57, 58, 59))
+    _, m, l = pmkl_pytorch_ext.fused_self_attention_fw(q, k, v, True)
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    dq, dk, dv = pmkl_pytorch_ext.fused_self_attention_bw(dout, q, k, v, m, l, True)
+    torch.cuda.synchronize()
+    grads = 3 * q.numel() * q.element_size()
+    ws = pmkl_b200.attention_bwd_workspace_size(B, H, S, D, torch.bfloat16)
+    assert torch.cuda.max_memory_allocated() - before <= grads + ws + (1 << 20)  # no input copies
+    assert dq.stride() == q.stride()  # gradients in their inputs' layout
+    ref = run_bwd_contiguous(dout, q, k, v, m, l, True)
+    for a, b in zip((dq, dk, dv), ref):
+        assert torch.equal(a, b)
+
+
+def test_autograd_grouped_query():
+    """fused_self_attention_ex: autograd through grouped-query K/V views."""
+    from pmkl_function import fused_self_attention_ex
+    B, H, Hkv, S, D = 1, 8, 2, 256, 128
+    q = randn((B, H, S, D), torch.bfloat16, 60).requires_grad_()
+    k, v = (bshd_view(B, Hkv, S, D, torch.bfloat16, s).detach().requires_grad_() for s in (61, 62))
+    out, m, l = fused_self_attention_ex(q, k, v, True)
+    dout = randn(out.shape, torch.bfloat16, 63)
+    out.backward(dout)
+    assert q.grad.shape == q.shape and k.grad.shape == k.shape and v.grad.shape == v.shape
+    ref = group_oracle(dout, q.detach(), k.detach(), v.detach(), m, l, True, H // Hkv)
+    assert_grads_close((q.grad, k.grad, v.grad), ref, torch.bfloat16, "autograd gqa")
+    fo, _, _ = oracle.attention_fwd(np32(q), np32(k).repeat(H // Hkv, axis=1), np32(v).repeat(H // Hkv, axis=1), True)
+    assert abs(np32(out) - fo).max() <= 2e-3 + 2.0 ** -8 * abs(fo).max()
