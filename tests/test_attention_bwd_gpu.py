@@ -4,10 +4,12 @@ called through the C ABI and checked against the CPU oracle's backward
 host_self_attention_backward (fused_self_attention.cpp:66-135) in
 tests/test_oracle.py.
 
-Tolerances (max |err| relative to the largest |gradient| of the tensor):
-  fp32 (CUDA-core path)          2e-5   -- fp32 rounding in a different order
-  fp16/bf16 (tensor-core path)   1e-2   -- P and dS are rounded to 16 bits before
-                                           the gradient products, the outputs once
+Tolerances (max |err| relative to the largest |gradient| of the tensor), set
+about 1.3x above the worst errors measured on B200 over this file and the
+layout tests (bf16 6.3e-3, fp16 2.3e-3, fp32 8.6e-7):
+  fp32 (CUDA-core path)          2e-6   -- fp32 rounding in a different order
+  bf16 (tensor-core path)        8e-3   -- P and dS are rounded to 16 bits before
+  fp16 (tensor-core path)        3e-3      the gradient products, the outputs once
                                            more; plus half an output ulp per value
 The 16-bit reference (the reference's own bf16 run accumulates every gradient in
 bf16) is further from the fp32 oracle than this bound; see test_oracle.py."""
@@ -26,7 +28,7 @@ SIMT = pmkl_b200.KERNEL_SIMT
 LP = [torch.bfloat16, torch.float16]
 BWD_F32 = sorted(p.stem for p in GOLDEN.glob("attn_bwd_*f32*.npz"))
 BWD_LP = sorted(p.stem for p in GOLDEN.glob("attn_bwd_*.npz") if "f32" not in p.stem)
-TOL = {torch.float32: 2e-5, torch.bfloat16: 1e-2, torch.float16: 1e-2}
+TOL = {torch.float32: 2e-6, torch.bfloat16: 8e-3, torch.float16: 3e-3}
 
 
 @pytest.fixture(autouse=True)
@@ -35,9 +37,14 @@ def _no_device_timeouts():
     assert pmkl_b200.device_error(clear=True) == 0, "a kernel abandoned a bounded wait"
 
 
+WORST = {}  # dtype name -> largest error relative to the gradient's max seen in this session
+
+
 def assert_grad_close(got: np.ndarray, ref: np.ndarray, dtype, what: str) -> float:
     scale = max(float(np.abs(ref).max()), 1e-30)
     err = np.abs(got.astype(np.float64) - ref)
+    key = str(dtype).replace("torch.", "")
+    WORST[key] = max(WORST.get(key, 0.0), float(np.nanmax(err)) / scale)
     bound = TOL[dtype] * scale
     if dtype != torch.float32:
         mant = 7 if dtype == torch.bfloat16 else 10
