@@ -55,7 +55,10 @@ WORKLOADS = {
     "attention": (16, 32, 4096, 128, "bfloat16", 1.0, True, "BASELINE config 3: causal self-attention bf16 B16 H32 S4096 D128"),
     "attention-cfg2": (8, 16, 1024, 64, "float16", 1.0, True, "BASELINE config 2: causal self-attention fp16 B8 H16 S1024 D64"),
     "attention-cfg4": (1, 32, 32768, 128, "bfloat16", 0.5, True, "BASELINE config 4: causal self-attention bf16 B1 H32 S32768 D128"),
+    "attention-cfg1": (2, 4, 128, 64, "float32", 1.0, True, "BASELINE config 1: causal self-attention fp32 B2 H4 S128 D64"),
     "softmax": (65536, 1024, None, None, "float32", 2.0, None, "BASELINE config 5: warp softmax fp32 65536 x 1024"),
+    "softmax-bf16": (65536, 1024, None, None, "bfloat16", 2.0, None,
+                     "warp softmax bf16 in / bf16 out 65536 x 1024 (the general kernel's path)"),
     "attention-bwd": (16, 32, 4096, 128, "bfloat16", 1.0, True,
                       "backward of BASELINE config 3: fused_self_attention_bw bf16 B16 H32 S4096 D128 causal"),
 }
@@ -365,7 +368,7 @@ def reference_record(name: str, wl, steps: int, warmup: int, budget_total_s: flo
     ctx = mp.get_context("spawn")
     total_steps = steps + warmup
     budget = max(0.5, min(20.0, budget_total_s / max(1, total_steps)))
-    if name == "softmax":
+    if name.startswith("softmax"):
         rows_total, el = B, H
         probe = _ref_softmax_worker((256, el, 0))
         rows = max(1, min(rows_total // cores if rows_total >= cores else rows_total, int(budget / (probe / 256))))
@@ -709,11 +712,13 @@ def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, c
     import pmkl_b200
 
     rows_all, el = wl[0], wl[1]
+    dt = getattr(torch, wl[4])
+    esz = torch.tensor([], dtype=dt).element_size()
     lo, hi = shard(rows_all, world, rank)
     rows = hi - lo
     dev = torch.device("cuda", local)
     g = torch.Generator(device=dev).manual_seed(args.seed + rank)
-    x = torch.randn(rows, el, generator=g, device=dev) * wl[5]
+    x = (torch.randn(rows, el, generator=g, device=dev) * wl[5]).to(dt)
     y = torch.empty_like(x)
     stream = torch.cuda.current_stream()
 
@@ -721,8 +726,8 @@ def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, c
         pmkl_b200.warp_softmax_fwd(y, x, el, el, rows, stream=stream)
 
     total_ms, per_ms, clocks = timed_loop(step, steps, args.warmup, world, sampler)
-    bytes_rank = 2.0 * rows * el * 4
-    bytes_all = 2.0 * rows_all * el * 4
+    bytes_rank = 2.0 * rows * el * esz
+    bytes_all = 2.0 * rows_all * el * esz
     t_max = max_over_ranks(total_ms, world)
     value = bytes_all * steps / (t_max / 1e3) / 1e9
     launch_avg = statistics.mean(per_ms)
@@ -760,7 +765,7 @@ def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, c
     e2e_value = bytes_all * e2e_steps / (max_over_ranks(e2e_ms, world) / 1e3) / 1e9
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and dt == torch.float32:
         try:
             # the whole problem (all rows_all rows), repeated for ~5 s of CPU work
             n = rows_all
@@ -776,23 +781,25 @@ def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, c
     return {
         "metric": SOFTMAX_METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": t_max / steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded N(0, 4) generated on device",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if esz == 4 else wl[4],
+        "data": "synthetic, seeded N(0, 4) generated on device",
         "config": {"workload": wl[7], "rows": rows_all, "elements": el, "parallelism": f"row shards over {world} GPU(s)",
-                   "l2": "256 MiB in + 256 MiB out per GPU at N=1 exceed the 126 MB L2; no flush"},
-        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": rows * el * 4,
-                "d2h_bytes_per_step": rows * el * 4, "api": "pmkl_warp_softmax_fwd (C ABI)", "steps": e2e_steps,
+                   "l2": "%.0f MiB in + out per GPU exceed the 126 MB L2; no flush" % (2 * rows * el * esz / 2**20)},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": rows * el * esz,
+                "d2h_bytes_per_step": rows * el * esz, "api": "pmkl_warp_softmax_fwd (C ABI)", "steps": e2e_steps,
                 "chunks": n_chunks, "overlap": "H2D / softmax / D2H of consecutive row chunks on three streams"},
         "gpu_launches": steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} copy bandwidth",
                      "traffic": (traffic * rows if traffic is not None else None),
-                     "algorithmic_bytes": bytes_rank, "kernel": "softmax_vec_kernel", "launch_ms_avg": launch_avg},
+                     "algorithmic_bytes": bytes_rank,
+                     "kernel": "softmax_vec_kernel" if esz == 4 else "softmax_gen_kernel", "launch_ms_avg": launch_avg},
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
 
 
-RUNNERS = {"softmax": run_softmax, "attention-bwd": run_attention_bwd}
+RUNNERS = {"softmax": run_softmax, "softmax-bf16": run_softmax, "attention-bwd": run_attention_bwd}
 
 
 def run_workload(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget):
@@ -805,8 +812,8 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.shape:
         dims = [int(x) for x in args.shape.split(",")]
-        if args.workload == "softmax":
-            wl = (dims[0], dims[1]) + wl[2:7] + (f"warp softmax fp32 {dims[0]} x {dims[1]} (profiling size)",)
+        if args.workload.startswith("softmax"):
+            wl = (dims[0], dims[1]) + wl[2:7] + (f"warp softmax {wl[4]} {dims[0]} x {dims[1]} (profiling size)",)
         else:
             wl = tuple(dims[:4]) + wl[4:7] + (f"causal self-attention {wl[4]} B{dims[0]} H{dims[1]} S{dims[2]} "
                                               f"D{dims[3]} (profiling size)",)
