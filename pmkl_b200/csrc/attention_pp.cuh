@@ -680,24 +680,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                         constexpr float kSpec = BF16 ? 30.0f : 15.0f;
                         const bool redo = (m_true - m_new) * c2 > kSpec;
                         if (__any_sync(0xffffffffu, redo)) {
-                            // Rare: scores 64-127 are reloaded (P went to the
-                            // columns of scores 0-63), scores 0-63 are still in
-                            // registers.
-                            if constexpr (D == 64) {
-                                // S is untouched by P here: reload every score.
-                                tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
-                                tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-                            }
-                            tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-                            tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
-                            tmem_wait_ld();
-                            if constexpr (D == 64) mask_half(0);
-                            mask_half(1);
                             if (redo) m_new = m_true;
                             nm2 = make_float2(-m_new * c2, -m_new * c2);
-                            tmem_wait_st();
                             float unused[4];
-                            r = exp_chunks<BF16, 0, 0, 128, false, D == 64>(s, c22, nm2, sa, false, unused, pbuf);
+                            if constexpr (D == 64) {
+                                // Rare.  S is untouched by P here (P waits in
+                                // registers): stream the scores back 32 at a
+                                // time into the deferred P words, so that the
+                                // path needs no more registers than the common one.
+                                r = make_float2(0.f, 0.f);
+#pragma unroll
+                                for (int c0 = 0; c0 < 128; c0 += 32) {
+                                    uint32_t w[32];
+                                    tmem_ld32(sa + c0, w);
+                                    tmem_wait_ld();
+                                    uint32_t ph[16];
+#pragma unroll
+                                    for (int i = 0; i < 16; ++i) {
+                                        float s0 = __uint_as_float(w[2 * i]), s1 = __uint_as_float(w[2 * i + 1]);
+                                        if (masked && c0 + 2 * i >= lim) s0 = -INFINITY;
+                                        if (masked && c0 + 2 * i + 1 >= lim) s1 = -INFINITY;
+                                        const float2 a = fma2(make_float2(s0, s1), c22, nm2);
+                                        const float2 e = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+                                        r = add2(r, e);
+                                        ph[i] = pack2<BF16>(e.x, e.y);
+                                    }
+#pragma unroll
+                                    for (int i = 0; i < 16; ++i) pbuf[c0 / 2 + i] = ph[i];
+                                }
+                            } else {
+                                // Rare: scores 64-127 are reloaded (P went to the
+                                // columns of scores 0-63), scores 0-63 are still in
+                                // registers.
+                                tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+                                tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+                                tmem_wait_ld();
+                                mask_half(1);
+                                tmem_wait_st();
+                                r = exp_chunks<BF16, 0, 0, 128, false, false>(s, c22, nm2, sa, false, unused, pbuf);
+                            }
                         }
                         rsum = r.x + r.y;
                         fac = (m_new == m_used) ? 1.f : ex2_approx((m_used - m_new) * c2);
