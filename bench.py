@@ -793,7 +793,7 @@ def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, c
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} copy bandwidth",
                      "traffic": (traffic * rows if traffic is not None else None),
                      "algorithmic_bytes": bytes_rank,
-                     "kernel": "softmax_vec_kernel" if esz == 4 else "softmax_gen_kernel", "launch_ms_avg": launch_avg},
+                     "kernel": "softmax_vec_kernel" if esz == 4 else "softmax_vec8_kernel", "launch_ms_avg": launch_avg},
         "clocks": clocks,
         "cpu_baseline": cpu,
     }

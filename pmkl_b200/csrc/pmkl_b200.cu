@@ -744,6 +744,49 @@ int launch_softmax_vec(float *dst, const float *src, int elements, int stride, i
     return launch_status();
 }
 
+template <typename TI, typename TO, bool LOG>
+int launch_softmax_vec8_t(void *dst, const void *src, int elements, int stride, int rows, cudaStream_t stream) {
+    const int v8 = (elements + 255) / 256;
+    const unsigned blocks = static_cast<unsigned>((rows + softmax::kThreads / 32 - 1) / (softmax::kThreads / 32));
+    TO *d = static_cast<TO *>(dst);
+    const TI *s = static_cast<const TI *>(src);
+    switch (v8) {
+        case 1:
+            softmax::softmax_vec8_kernel<TI, TO, 1, LOG><<<blocks, softmax::kThreads, 0, stream>>>(d, s, elements, stride, rows);
+            break;
+        case 2:
+            softmax::softmax_vec8_kernel<TI, TO, 2, LOG><<<blocks, softmax::kThreads, 0, stream>>>(d, s, elements, stride, rows);
+            break;
+        case 3:
+            softmax::softmax_vec8_kernel<TI, TO, 3, LOG><<<blocks, softmax::kThreads, 0, stream>>>(d, s, elements, stride, rows);
+            break;
+        case 4:
+            softmax::softmax_vec8_kernel<TI, TO, 4, LOG><<<blocks, softmax::kThreads, 0, stream>>>(d, s, elements, stride, rows);
+            break;
+        default:
+            return PMKL_ERR_INVALID_SHAPE;
+    }
+    return launch_status();
+}
+
+template <typename TI, bool LOG>
+int launch_softmax_vec8_out(void *dst, const void *src, int elements, int stride, int rows, int out_dtype,
+                            cudaStream_t stream) {
+    if (out_dtype == PMKL_DTYPE_F32) return launch_softmax_vec8_t<TI, float, LOG>(dst, src, elements, stride, rows, stream);
+    if (out_dtype == PMKL_DTYPE_F16) return launch_softmax_vec8_t<TI, __half, LOG>(dst, src, elements, stride, rows, stream);
+    return launch_softmax_vec8_t<TI, __nv_bfloat16, LOG>(dst, src, elements, stride, rows, stream);
+}
+
+template <bool LOG>
+int launch_softmax_vec8(void *dst, const void *src, int elements, int stride, int rows, int in_dtype, int out_dtype,
+                        cudaStream_t stream) {
+    if (in_dtype == PMKL_DTYPE_F32)
+        return launch_softmax_vec8_out<float, LOG>(dst, src, elements, stride, rows, out_dtype, stream);
+    if (in_dtype == PMKL_DTYPE_F16)
+        return launch_softmax_vec8_out<__half, LOG>(dst, src, elements, stride, rows, out_dtype, stream);
+    return launch_softmax_vec8_out<__nv_bfloat16, LOG>(dst, src, elements, stride, rows, out_dtype, stream);
+}
+
 template <bool LOG>
 int launch_softmax_gen(void *dst, const void *src, int elements, int stride, int rows, int in_dtype, int out_dtype,
                        cudaStream_t stream) {
@@ -934,6 +977,11 @@ int pmkl_warp_softmax_fwd(void *dst, const void *src, int elements, int stride, 
                       : launch_softmax_vec<false>(static_cast<float *>(dst), static_cast<const float *>(src),
                                                   elements, stride, rows, stream);
     }
+    // Other dtype pairs: 8-element vectors when rows allow them.
+    const bool vec8 = (elements % 8) == 0 && (stride % 8) == 0 && aligned16(dst) && aligned16(src);
+    if (vec8)
+        return is_log ? launch_softmax_vec8<true>(dst, src, elements, stride, rows, in_dtype, out_dtype, stream)
+                      : launch_softmax_vec8<false>(dst, src, elements, stride, rows, in_dtype, out_dtype, stream);
     return is_log ? launch_softmax_gen<true>(dst, src, elements, stride, rows, in_dtype, out_dtype, stream)
                   : launch_softmax_gen<false>(dst, src, elements, stride, rows, in_dtype, out_dtype, stream);
 }

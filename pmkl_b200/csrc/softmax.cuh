@@ -11,6 +11,9 @@
 //     result in every lane (no shared memory, no block barrier), and the
 //     results go out with 16-byte streaming stores.  Bandwidth-bound: one
 //     read and one write of every element.
+//   * 8-element vector path (any dtype pair; elements and stride multiples of
+//     8, 16-byte aligned rows): the same with 16-byte loads of eight 16-bit
+//     values, converted to fp32 in registers and back on the store.
 //   * general path (any dtype pair, any stride/alignment): the reference's
 //     shape -- 2^L elements per row padded with -inf, min(2^L, 32) lanes per
 //     row, coalesced scalar loads -- with shuffle-only reductions.
@@ -94,6 +97,110 @@ __global__ void __launch_bounds__(kThreads)
         for (int i = 0; i < VPL; ++i) {
             const int idx = lane + 32 * i;
             if (idx < n4) st_stream(d4 + idx, make_float4(x[i].x * inv, x[i].y * inv, x[i].z * inv, x[i].w * inv));
+        }
+    }
+}
+
+// Eight consecutive elements of a row as fp32: one 16-byte load for 16-bit
+// types, two for fp32 (non-caching, the row is read once).
+template <typename T>
+__device__ __forceinline__ void load8(const T *p, float (&v)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 a = ld_stream(reinterpret_cast<const float4 *>(p));
+        const float4 b = ld_stream(reinterpret_cast<const float4 *>(p) + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+        uint32_t w[4];
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                     : "l"(p));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float lo, hi;
+            if constexpr (std::is_same<T, __half>::value) {
+                const __half2 h = *reinterpret_cast<const __half2 *>(&w[i]);
+                lo = __low2float(h), hi = __high2float(h);
+            } else {
+                lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xffff0000u);
+            }
+            v[2 * i] = lo, v[2 * i + 1] = hi;
+        }
+    }
+}
+
+// Eight fp32 values stored as T (round to nearest), streaming stores.
+template <typename T>
+__device__ __forceinline__ void store8(T *p, const float (&v)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        st_stream(reinterpret_cast<float4 *>(p), make_float4(v[0], v[1], v[2], v[3]));
+        st_stream(reinterpret_cast<float4 *>(p) + 1, make_float4(v[4], v[5], v[6], v[7]));
+    } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (std::is_same<T, __half>::value) {
+                const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t *>(&h);
+            } else {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t *>(&h);
+            }
+        }
+        asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                     "r"(w[3])
+                     : "memory");
+    }
+}
+
+// Vector path for any dtype pair: one warp per row, 8-element vectors (16 bytes
+// of 16-bit data), V8 vectors per lane (elements <= 256 * V8, a multiple of 8;
+// 16-byte aligned rows), fp32 accumulation, shuffle-only reductions.
+template <typename TI, typename TO, int V8, bool LOG>
+__global__ void __launch_bounds__(kThreads)
+    softmax_vec8_kernel(TO *__restrict__ dst, const TI *__restrict__ src, int elements, long long stride, int rows) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long row = static_cast<long long>(blockIdx.x) * (kThreads / 32) + warp;
+    if (row >= rows) return;
+    const TI *s = src + row * stride;
+    TO *d = dst + row * stride;
+    const int n8 = elements >> 3;
+    float x[V8][8];
+#pragma unroll
+    for (int i = 0; i < V8; ++i) {
+        const int idx = lane + 32 * i;
+        if (idx < n8) {
+            load8(s + 8 * idx, x[i]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[i][e] = -INFINITY;
+        }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < V8; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, x[i][e]);
+    mx = group_max<32>(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < V8; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float ev = expf(x[i][e] - mx);
+            sum += ev;
+            if (!LOG) x[i][e] = ev;
+        }
+    sum = group_sum<32>(sum);
+    const float sub = LOG ? mx + logf(sum) : 0.f;
+    const float inv = (sum == 0.f) ? __int_as_float(0x7fc00000) : 1.f / sum;
+#pragma unroll
+    for (int i = 0; i < V8; ++i) {
+        const int idx = lane + 32 * i;
+        if (idx < n8) {
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[e] = LOG ? x[i][e] - sub : x[i][e] * inv;
+            store8(d + 8 * idx, y);
         }
     }
 }

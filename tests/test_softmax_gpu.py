@@ -88,14 +88,31 @@ def test_vector_path_variants(is_log):
 
 @pytest.mark.parametrize("in_dt,out_dt", [(torch.float16, torch.float16), (torch.bfloat16, torch.bfloat16),
                                           (torch.bfloat16, torch.float32), (torch.float16, torch.float32),
-                                          (torch.float32, torch.bfloat16)])
-def test_dtypes(in_dt, out_dt):
-    rows, el = 65, 1000
-    x = (torch.randn(rows * el, generator=torch.Generator().manual_seed(4)) * 2).to(in_dt)
-    y = run(x, el, el, rows, out_dtype=out_dt)
-    ref = oracle.softmax_fwd(x.float().numpy(), elements=el, stride=el, rows=rows)
+                                          (torch.float32, torch.bfloat16), (torch.float32, torch.float16)])
+@pytest.mark.parametrize("el", [1000, 1024, 256, 1003, 24])
+@pytest.mark.parametrize("is_log", [False, True])
+def test_dtypes(in_dt, out_dt, el, is_log):
+    """16-bit input or output: rows whose length and stride are multiples of 8
+    take the 8-element vector kernel, the others the general kernel; both
+    match the oracle to the output type's rounding."""
+    rows = 65
+    x = (torch.randn(rows * el, generator=torch.Generator().manual_seed(4 + el)) * 2).to(in_dt)
+    y = run(x, el, el, rows, out_dtype=out_dt, is_log=is_log)
+    ref = oracle.softmax_fwd(x.float().numpy(), elements=el, stride=el, rows=rows, is_log=is_log)
     tol = 1e-5 if out_dt == torch.float32 else (2.0 ** -8 if out_dt == torch.bfloat16 else 2.0 ** -11)
-    assert np.abs(y - ref).max() <= tol + 1e-6
+    assert (np.abs(y - ref) <= tol * np.maximum(1.0, np.abs(ref)) + 1e-6).all()
+
+
+def test_16bit_strided_rows_and_misalignment():
+    """bf16 rows with a stride of 1032 (a multiple of 8: vector kernel) and the
+    same data one element off a 16-byte boundary (general kernel)."""
+    rows, el, st = 300, 1024, 1032
+    x = (torch.randn(rows * st + 8, generator=torch.Generator().manual_seed(6)) * 2).to(torch.bfloat16)
+    ref = oracle.softmax_fwd(x.float().numpy()[:rows * st], elements=el, stride=st, rows=rows)
+    y = run(x[:rows * st], el, st, rows, out_dtype=torch.bfloat16)
+    assert np.abs(valid(y, el, st, rows) - valid(ref, el, st, rows)).max() <= 2.0 ** -8
+    y2 = run(x[:rows * st], el, st, rows, out_dtype=torch.bfloat16, src_offset=1, dst_offset=1)
+    assert np.abs(valid(y2, el, st, rows) - valid(ref, el, st, rows)).max() <= 2.0 ** -8
 
 
 def test_rows_sum_to_one_and_nan_rows():
