@@ -101,6 +101,12 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+__device__ __forceinline__ float ptx_ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Eight consecutive elements of a row as fp32: one 16-byte load for 16-bit
 // types, two for fp32 (non-caching, the row is read once).
 template <typename T>
@@ -181,12 +187,18 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx = fmaxf(mx, x[i][e]);
     mx = group_max<32>(mx);
+    // With a 16-bit output the hardware exp2 on (x - max) log2 e is far more
+    // precise than the stored value (2^-9 / 2^-12 relative); fp32 outputs keep
+    // the accurate expf of the reference's fp32 path.
+    constexpr bool kFastExp = sizeof(TO) == 2;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float mxl = mx * kLog2e;
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < V8; ++i)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const float ev = expf(x[i][e] - mx);
+            const float ev = kFastExp ? ptx_ex2(fmaf(x[i][e], kLog2e, -mxl)) : expf(x[i][e] - mx);
             sum += ev;
             if (!LOG) x[i][e] = ev;
         }

@@ -331,3 +331,32 @@ def test_autograd_grouped_query():
     assert_grads_close((q.grad, k.grad, v.grad), ref, torch.bfloat16, "autograd gqa")
     fo, _, _ = oracle.attention_fwd(np32(q), np32(k).repeat(H // Hkv, axis=1), np32(v).repeat(H // Hkv, axis=1), True)
     assert abs(np32(out) - fo).max() <= 2e-3 + 2.0 ** -8 * abs(fo).max()
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("S", [1, 77, 300])
+def test_bwd_multi_query_ragged(S, causal):
+    """Multi-query (one K/V head for 8 query heads), ragged and tiny S, causal
+    and not: the dK/dV kernel's group loop over partial tiles."""
+    B, H, D = 2, 8, 128
+    q, dout = (randn((B, H, S, D), torch.bfloat16, s) for s in (70, 71))
+    k, v = (randn((B, 1, S, D), torch.bfloat16, s) for s in (72, 73))
+    m, l = stats(q, k, v, causal)
+    got = run_bwd_strided(dout, q, k, v, m, l, causal)
+    ref = group_oracle(dout, q, k, v, m, l, causal, H)
+    assert_grads_close(got, ref, torch.bfloat16, f"mqa S{S} causal={causal}")
+
+
+def test_extension_grouped_query_backward_entry():
+    """fused_self_attention_bw_ex with fewer K/V heads returns dk, dv with k's
+    and v's shape (fp16, head size 64, [B, S, H, D] views)."""
+    B, H, Hkv, S, D = 2, 6, 3, 333, 64
+    q, dout = (bshd_view(B, H, S, D, torch.float16, s) for s in (74, 75))
+    k, v = (bshd_view(B, Hkv, S, D, torch.float16, s) for s in (76, 77))
+    out, m, l = pmkl_pytorch_ext.fused_self_attention_fw_ex(q, k, v, True)
+    dq, dk, dv = pmkl_pytorch_ext.fused_self_attention_bw_ex(dout, q, k, v, m, l, True)
+    assert dq.shape == q.shape and dk.shape == k.shape and dv.shape == v.shape
+    ref = group_oracle(dout, q, k, v, m, l, True, H // Hkv)
+    assert_grads_close((dq, dk, dv), ref, torch.float16, "ext gqa")
+    with pytest.raises(RuntimeError, match="shapes must match"):
+        pmkl_pytorch_ext.fused_self_attention_bw(dout, q, k, v, m, l, True)  # reference API: equal heads only
