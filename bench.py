@@ -61,6 +61,10 @@ WORKLOADS = {
                      "warp softmax bf16 in / bf16 out 65536 x 1024 (the general kernel's path)"),
     "attention-bwd": (16, 32, 4096, 128, "bfloat16", 1.0, True,
                       "backward of BASELINE config 3: fused_self_attention_bw bf16 B16 H32 S4096 D128 causal"),
+    "softmax-gen": (65536, 1023, None, None, "float32", 2.0, None,
+                    "warp softmax fp32 65536 x 1023 (odd row length: the general kernel's path)"),
+    "attention-bwd-fp32": (8, 32, 2048, 64, "float32", 1.0, True,
+                           "backward fp32 B8 H32 S2048 D64 causal (the CUDA-core backward's path)"),
 }
 BWD_METRIC = "causal attention backward TFLOP/s (whole box)"
 
@@ -376,7 +380,7 @@ def reference_record(name: str, wl, steps: int, warmup: int, budget_total_s: flo
         unit_per_step = cores * rows * el * 8.0 / 1e9  # GB moved per step (read + write fp32)
         unit, metric = "GB/s", SOFTMAX_METRIC
         sample = f"reference host_softmax_forward (CPU fp32), {rows} rows x {el} per core per step"
-    elif name == "attention-bwd":
+    elif name.startswith("attention-bwd"):
         r = pick_bwd_rows(D, dtype_name, causal, budget)
         work = [(r, D, dtype_name, std, causal, 100 + i) for i in range(cores)]
         unit_per_step = cores * attn_bwd_flops_per_slice(r, D, causal) / 1e12
@@ -390,8 +394,8 @@ def reference_record(name: str, wl, steps: int, warmup: int, budget_total_s: flo
         unit, metric = "TFLOP/s", ATTN_METRIC
         sample = (f"reference fused_self_attention_fw (CPU, {dtype_name}): per step each of {cores} worker "
                   f"processes runs a causal prefix of {r} of {S} rows of one (b,h) slice, D={D}")
-    fn = {"softmax": _ref_softmax_worker, "attention-bwd": _ref_attention_bwd_worker}.get(name,
-                                                                                          _ref_attention_worker)
+    fn = (_ref_softmax_worker if name.startswith("softmax") else
+          _ref_attention_bwd_worker if name.startswith("attention-bwd") else _ref_attention_worker)
     times = []
     with ctx.Pool(cores) as pool:
         for i in range(total_steps):
@@ -602,6 +606,7 @@ def run_attention_bwd(args, name, wl, rank, world, local, sampler, steps, e2e_st
 
     B, H, S, D, dtype_name, std, causal, desc = wl
     dt = getattr(torch, dtype_name)
+    simt = dtype_name == "float32" or D not in (64, 128)  # the CUDA-core backward
     n_slices = B * H
     lo, hi = shard(n_slices, world, rank)
     ns = hi - lo
@@ -693,17 +698,30 @@ def run_attention_bwd(args, name, wl, rank, world, local, sampler, steps, e2e_st
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "pmkl_pytorch_ext.fused_self_attention_bw", "steps": e2e_steps,
                 "chunks": n_chunks, "overlap": "H2D / backward / D2H of consecutive chunks on three streams"},
-        "gpu_launches": (4 if args.kernel == 3 else 3) * steps,
+        "gpu_launches": (2 if simt else 4 if args.kernel == 3 else 3) * steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"],
                      "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
                      "traffic": None,
-                     "kernel": "one backward call: attn_fwd_pp_kernel (delta epilogue) + attn_bwd_dq_kernel + "
-                               "attn_bwd_dkv_kernel",
+                     "kernel": ("one backward call: attn_bwd_simt_q_kernel + attn_bwd_simt_kv_kernel (CUDA cores)"
+                                if simt else "one backward call: attn_fwd_pp_kernel (delta epilogue) + "
+                                "attn_bwd_dq_kernel + attn_bwd_dkv_kernel"),
+                     "note": ("fp32 on CUDA cores: the bf16 tensor peak is context, not this path's bound"
+                              if simt else None),
                      "launch_ms_avg": launch_avg},
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+
+
+def softmax_kernel_name(esz: int, el: int) -> str:
+    """The kernel pmkl_warp_softmax_fwd picks for contiguous, aligned rows of
+    `el` elements with input and output of one dtype of `esz` bytes."""
+    if esz == 4 and el % 4 == 0:
+        return "softmax_vec_kernel"
+    if el % 8 == 0:
+        return "softmax_vec8_kernel"
+    return "softmax_gen_kernel"
 
 
 def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget):
@@ -793,13 +811,14 @@ def run_softmax(args, name, wl, rank, world, local, sampler, steps, e2e_steps, c
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} copy bandwidth",
                      "traffic": (traffic * rows if traffic is not None else None),
                      "algorithmic_bytes": bytes_rank,
-                     "kernel": "softmax_vec_kernel" if esz == 4 else "softmax_vec8_kernel", "launch_ms_avg": launch_avg},
+                     "kernel": softmax_kernel_name(esz, el), "launch_ms_avg": launch_avg},
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
 
 
-RUNNERS = {"softmax": run_softmax, "softmax-bf16": run_softmax, "attention-bwd": run_attention_bwd}
+RUNNERS = {"softmax": run_softmax, "softmax-bf16": run_softmax, "softmax-gen": run_softmax,
+           "attention-bwd": run_attention_bwd, "attention-bwd-fp32": run_attention_bwd}
 
 
 def run_workload(args, name, wl, rank, world, local, sampler, steps, e2e_steps, cpu_budget):
