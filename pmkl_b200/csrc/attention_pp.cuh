@@ -276,6 +276,9 @@ __device__ __forceinline__ float2 exp_chunks(const float (&s)[128], float2 c22, 
 
 // Pairs per 32-key chunk whose exp2 runs on the FMA pipe (0..16); the rest
 // use the MUFU unit.  A build-time knob, tuned on B200.
+#ifndef PMKL_PP_PREFETCH_NEXT
+#define PMKL_PP_PREFETCH_NEXT 1
+#endif
 #ifndef PMKL_PP_NPOLY
 #define PMKL_PP_NPOLY 0
 #endif
@@ -320,6 +323,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int wg = warp >> 2;
+    // Warp-wide waits (softmax and epilogue warps).  Head size 128: every lane
+    // tests the barrier and the warp agrees by vote (B200, config 3: 994 ->
+    // 1054 TFLOP/s against lane 0 waiting alone and broadcasting); head size
+    // 64: lane 0 waits alone (the all-lane form measured 2-4 % slower there).
+    auto wait_warp = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if constexpr (D == 128)
+            return mbar_wait_warp_all(bar, parity, abort_flag);
+        else
+            return mbar_wait_warp(bar, parity, abort_flag);
+    };
 
     if (threadIdx.x == 0) {
         for (int x = 0; x < 2; ++x) {
@@ -385,6 +398,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 };
                 if (w.act[0]) load_q(0, qc0);
                 if (w.act[1]) load_q(1, qc1);
+#if PMKL_PP_PREFETCH_NEXT
+                // The next unit's Q tiles (read once, from HBM) and its first K
+                // and V tiles are pulled into L2 now, a unit ahead, so that the
+                // loads at the unit boundary are served from L2.
+                if (k + 1 < p.n_rounds) {
+                    const int un = unit_of(p, k + 1);
+                    if (un < p.n_units) {
+                        const Unit wn = decode(p, un);
+                        const int bn = wn.bh / p.H;
+                        const int hn = wn.bh - bn * p.H;
+#pragma unroll
+                        for (int b = 0; b < C::kBoxes; ++b) {
+                            tma_prefetch_l2_4d(&tm_q, b * kBoxCols, wn.row0, hn, bn);
+                            if (wn.act[1]) tma_prefetch_l2_4d(&tm_q, b * kBoxCols, wn.row0 + 128, hn, bn);
+                            tma_prefetch_l2_4d(&tm_k, b * kBoxCols, 0, hn / p.kv_group, bn);
+                            tma_prefetch_l2_4d(&tm_v, b * kBoxCols, 0, hn / p.kv_group, bn);
+                        }
+                    }
+                }
+#endif
                 // One K or V tile into the next ring stage.
                 auto load_kv = [&](const int kv, const int jt) {
                     if (!ok) return;
@@ -617,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bool any_fac;
                     if (j == 0) {
                         // First key tile of the row: the maximum comes first.
-                        if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
+                        if (!(ok = wait_warp(&s_full[x], sc & 1))) break;
                         ++sc;
                         tc_fence_after();
                         float mx8[8];
@@ -662,7 +695,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         m_new = ((m_true - m_used) * c2 > 8.0f) ? m_true : m_used;
                         const float2 c22 = make_float2(c2, c2);
                         float2 nm2 = make_float2(-m_new * c2, -m_new * c2);
-                        if (!(ok = mbar_wait_warp(&s_full[x], sc & 1, abort_flag))) break;
+                        // Whether O and l move to a new reference this step is
+                        // known before S arrives; the vote is off the path from
+                        // the last exp to P's release.
+                        any_fac = __any_sync(0xffffffffu, m_new != m_used);
+                        if (!(ok = wait_warp(&s_full[x], sc & 1))) break;
                         ++sc;
                         tc_fence_after();
                         tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
@@ -681,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const bool redo = (m_true - m_new) * c2 > kSpec;
                         if (__any_sync(0xffffffffu, redo)) {
                             if (redo) m_new = m_true;
+                            any_fac = __any_sync(0xffffffffu, m_new != m_used);
                             nm2 = make_float2(-m_new * c2, -m_new * c2);
                             float unused[4];
                             if constexpr (D == 64) {
@@ -721,8 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
                         rsum = r.x + r.y;
-                        fac = (m_new == m_used) ? 1.f : ex2_approx((m_used - m_new) * c2);
-                        any_fac = __any_sync(0xffffffffu, m_new != m_used);
+                        fac = 1.f;  // the rare rescale below sets the factor
                     }
                     if constexpr (D == 64) {
                         // S_X may be overwritten from here on; P goes to its own
@@ -731,7 +768,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&s_read[x]);
-                        if (pvc > 0 && !(ok = mbar_wait_warp(&pv_done[x], (pvc - 1) & 1, abort_flag))) break;
+                        if (pvc > 0 && !(ok = wait_warp(&pv_done[x], (pvc - 1) & 1))) break;
                         ++pvc;
                         tc_fence_after();
                         tmem_st32(lane_base + col_p64(x), *reinterpret_cast<uint32_t(*)[32]>(pbuf));
@@ -740,6 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // O_X is idle here (head size 128: S_X(j) was issued after PV_X(j-1),
                     // and its commit covers every earlier MMA).
                     if (any_fac) {
+                        fac = (m_new == m_used) ? 1.f : ex2_approx((m_used - m_new) * c2);
 #pragma unroll
                         for (int cc = 0; cc < D / 32; ++cc) {
                             uint32_t o[32];
@@ -750,16 +788,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_st32(lane_base + col_o(x) + cc * 32, o);
                         }
                     }
-                    l = l * fac + rsum;
-                    m_used = m_new;
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&p_full[x]);
+                    // Row-sum bookkeeping after P is released.
+                    l = l * fac + rsum;
+                    m_used = m_new;
                 }
                 if (!ok) break;
                 // Row statistics for the epilogue.
-                if (uc > 0 && !(ok = mbar_wait_warp(&st_empty[x], (uc - 1) & 1, abort_flag))) break;
+                if (uc > 0 && !(ok = wait_warp(&st_empty[x], (uc - 1) & 1))) break;
                 sStats[(x * 3 + 0) * 128 + r_local] = m_used;
                 sStats[(x * 3 + 1) * 128 + r_local] = m_true;
                 sStats[(x * 3 + 2) * 128 + r_local] = l;
@@ -786,8 +825,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int x = 0; x < 2 && ok; ++x) {
                     if (!(x ? w.act[1] : w.act[0])) continue;
                     const uint32_t ocx = x ? oc1 : oc0;
-                    if (!(ok = mbar_wait_warp(&o_full[x], ocx & 1, abort_flag))) break;
-                    if (!(ok = mbar_wait_warp(&st_full[x], ocx & 1, abort_flag))) break;
+                    if (!(ok = wait_warp(&o_full[x], ocx & 1))) break;
+                    if (!(ok = wait_warp(&st_full[x], ocx & 1))) break;
                     if (x) ++oc1; else ++oc0;
                     tc_fence_after();
                     const float m_used = sStats[(x * 3 + 0) * 128 + r_local];
@@ -868,7 +907,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int b = 0; b < C::kBoxes; ++b) {
                             // The staging box is free once the previous TMA store has read it.
-                            if (nb > 0 && !(ok = mbar_wait_warp(stg_free, (nb - 1) & 1, abort_flag))) break;
+                            if (nb > 0 && !(ok = wait_warp(stg_free, (nb - 1) & 1))) break;
                             uint8_t *box = sStage + r_local * 128;
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {

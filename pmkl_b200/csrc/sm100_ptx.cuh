@@ -101,6 +101,15 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, v
     return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+// Warp-uniform form in which every lane tests the barrier and the warp agrees
+// by vote, so that a wake-up needs no broadcast from lane 0; the bounded wait
+// of lane 0 (mbar_wait_warp) takes over while the phase is still open.
+__device__ __forceinline__ bool mbar_wait_warp_all(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    for (int spin = 0; spin < 8; ++spin)
+        if (__all_sync(0xffffffffu, mbar_try_wait_suspend(bar, parity))) return true;
+    return mbar_wait_warp(bar, parity, abort_flag);
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -125,6 +134,15 @@ __device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *m
         " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
         : "memory");
+}
+
+// Brings one box of a 4-D tensor map into L2 (no shared memory, no barrier),
+// so that a later tma_load_4d of the same box is served from L2.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap *map, int x, int y, int z, int w) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z), "r"(w)
+                 : "memory");
 }
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *smem_src, int x, int y, int z,
