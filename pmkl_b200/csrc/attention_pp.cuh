@@ -323,15 +323,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int wg = warp >> 2;
-    // Warp-wide waits (softmax and epilogue warps).  Head size 128: every lane
-    // tests the barrier and the warp agrees by vote (B200, config 3: 994 ->
-    // 1054 TFLOP/s against lane 0 waiting alone and broadcasting); head size
-    // 64: lane 0 waits alone (the all-lane form measured 2-4 % slower there).
+    // Warp-wide waits (softmax and epilogue warps): every lane tests the
+    // barrier and the warp agrees by vote, with no single-lane wait and
+    // broadcast on a tile's chain (B200, config 3: 994 -> 1054 TFLOP/s).  Head
+    // size 128 parks the warp with suspend-hinted tests; head size 64 polls
+    // (parking measured 2-4 % slower there, polling 4-8 % faster).
     auto wait_warp = [&](uint64_t *bar, uint32_t parity) -> bool {
         if constexpr (D == 128)
             return mbar_wait_warp_all(bar, parity, abort_flag);
         else
-            return mbar_wait_warp(bar, parity, abort_flag);
+            return mbar_wait_warp_poll(bar, parity, abort_flag);
     };
 
     if (threadIdx.x == 0) {
@@ -339,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&q_full[x], 1);
             mbar_init(&q_empty[x], 1);
             mbar_init(&s_full[x], 1);
-            mbar_init(&p_full[x], 4);
+            mbar_init(&p_full[x], 128);  // every softmax thread releases its own P row
             mbar_init(&o_full[x], 1);
             mbar_init(&o_empty[x], 4);
             mbar_init(&st_full[x], 4);
@@ -639,6 +640,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float s[128];
                     uint32_t pbuf[64];  // head size 64: P (hi) until the P buffer is free
                     uint32_t *sr = reinterpret_cast<uint32_t *>(s);
+                    auto mask_range = [&](const int c0, const int c1) {
+                        if (masked) {
+#pragma unroll
+                            for (int c = c0; c < c1; ++c)
+                                if (c >= lim) s[c] = -INFINITY;
+                        }
+                    };
                     auto mask_half = [&](const int h) {
                         if (masked) {
 #pragma unroll
@@ -702,17 +710,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!(ok = wait_warp(&s_full[x], sc & 1))) break;
                         ++sc;
                         tc_fence_after();
-                        tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
-                        tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-                        tmem_wait_ld();
-                        tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-                        tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
-                        mask_half(0);
                         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-                        float2 r = exp_chunks<BF16, NPOLY, 0, 64, true, D == 64>(s, c22, nm2, sa, !masked, mx, pbuf);
-                        tmem_wait_ld();
-                        mask_half(1);
-                        r = add2(r, exp_chunks<BF16, NPOLY, 64, 128, true, D == 64>(s, c22, nm2, sa, !masked, mx, pbuf));
+                        float2 r;
+                        if constexpr (D == 128) {
+                            // The exps start once scores 0-31 are in registers;
+                            // the other 96 load meanwhile.  P of keys 0-31 goes to
+                            // columns whose scores have been read.
+                            tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                            tmem_wait_ld();
+                            tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                            tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+                            tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+                            mask_range(0, 32);
+                            r = exp_chunks<BF16, NPOLY, 0, 32, true, false>(s, c22, nm2, sa, !masked, mx, pbuf);
+                            tmem_wait_ld();
+                            mask_range(32, 128);
+                            r = add2(r, exp_chunks<BF16, NPOLY, 32, 128, true, false>(s, c22, nm2, sa, !masked, mx, pbuf));
+                        } else {
+                            tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                            tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                            tmem_wait_ld();
+                            tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+                            tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+                            mask_half(0);
+                            r = exp_chunks<BF16, NPOLY, 0, 64, true, true>(s, c22, nm2, sa, !masked, mx, pbuf);
+                            tmem_wait_ld();
+                            mask_half(1);
+                            r = add2(r, exp_chunks<BF16, NPOLY, 64, 128, true, true>(s, c22, nm2, sa, !masked, mx, pbuf));
+                        }
                         m_true = fmaxf(m_true, fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]));
                         constexpr float kSpec = BF16 ? 30.0f : 15.0f;
                         const bool redo = (m_true - m_new) * c2 > kSpec;
@@ -788,10 +813,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_st32(lane_base + col_o(x) + cc * 32, o);
                         }
                     }
+                    // Every thread releases its own row (its release covers its own
+                    // P stores), so no warp barrier or single-lane branch sits
+                    // between the last P store and the arrive.
                     tmem_wait_st();
                     tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&p_full[x]);
+                    mbar_arrive(&p_full[x]);
                     // Row-sum bookkeeping after P is released.
                     l = l * fac + rsum;
                     m_used = m_new;

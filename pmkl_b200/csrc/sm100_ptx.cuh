@@ -110,6 +110,14 @@ __device__ __forceinline__ bool mbar_wait_warp_all(uint64_t *bar, uint32_t parit
     return mbar_wait_warp(bar, parity, abort_flag);
 }
 
+// Warp-uniform polling form: every lane tests the barrier without parking
+// for a while (a few thousand tests), then lane 0's bounded wait takes over.
+__device__ __forceinline__ bool mbar_wait_warp_poll(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    for (int spin = 0; spin < 4096; ++spin)
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    return mbar_wait_warp(bar, parity, abort_flag);
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
