@@ -63,3 +63,19 @@ def test_every_workload_has_a_runner(name):
     assert callable(fn)
     if name.startswith("softmax"):
         assert fn is bench.run_softmax
+
+
+def test_softmax_kernel_name_follows_the_dispatch_rule():
+    # pmkl_warp_softmax_fwd: fp32 rows of multiples of 4 -> 16-byte vectors;
+    # other dtypes with rows of multiples of 8 -> 8-element vectors; else general
+    assert bench.softmax_kernel_name(4, 1024) == "softmax_vec_kernel"
+    assert bench.softmax_kernel_name(4, 1023) == "softmax_gen_kernel"
+    assert bench.softmax_kernel_name(2, 1024) == "softmax_vec8_kernel"
+    assert bench.softmax_kernel_name(2, 1020) == "softmax_gen_kernel"
+
+
+def test_extra_workloads_have_runners():
+    for name in ("softmax-gen", "attention-bwd-fp32", "softmax-bf16", "attention-bwd"):
+        assert name in bench.WORKLOADS and name in bench.RUNNERS
+    # the reference arm's attention-bwd family shares one worker
+    assert bench.WORKLOADS["attention-bwd-fp32"][4] == "float32"
