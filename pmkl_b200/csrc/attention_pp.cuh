@@ -342,9 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&s_full[x], 1);
             mbar_init(&p_full[x], 128);  // every softmax thread releases its own P row
             mbar_init(&o_full[x], 1);
-            mbar_init(&o_empty[x], 4);
-            mbar_init(&st_full[x], 4);
-            mbar_init(&st_empty[x], 4);
+            mbar_init(&o_empty[x], 128);  // hand-offs between warpgroups: one arrival per thread
+            mbar_init(&st_full[x], 128);
+            mbar_init(&st_empty[x], 128);
             mbar_init(&s_read[x], 4);
             mbar_init(&pv_done[x], 1);
         }
@@ -829,8 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sStats[(x * 3 + 0) * 128 + r_local] = m_used;
                 sStats[(x * 3 + 1) * 128 + r_local] = m_true;
                 sStats[(x * 3 + 2) * 128 + r_local] = l;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&st_full[x]);
+                mbar_arrive(&st_full[x]);
                 ++uc;
             }
         }
@@ -859,8 +858,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float m_used = sStats[(x * 3 + 0) * 128 + r_local];
                     const float m_true = sStats[(x * 3 + 1) * 128 + r_local];
                     const float l = sStats[(x * 3 + 2) * 128 + r_local];
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&st_empty[x]);
+                    mbar_arrive(&st_empty[x]);
                     const float inv_l = 1.f / l;
                     const int row = w.row0 + 128 * x + r_local;
                     const uint32_t oa = lane_base + col_o(x);
@@ -880,8 +878,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_wait_ld();
                             if (cc == D / 32 - 1) {
                                 tc_fence_before();
-                                __syncwarp();
-                                if (lane == 0) mbar_arrive(&o_empty[x]);
+                                mbar_arrive(&o_empty[x]);
                             }
                             if (row < p.S) {
 #pragma unroll
@@ -918,8 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_wait_ld();
                             if (cc == D / 32 - 1) {
                                 tc_fence_before();
-                                __syncwarp();
-                                if (lane == 0) mbar_arrive(&o_empty[x]);
+                                mbar_arrive(&o_empty[x]);
                             }
                             if (row < p.S) {
 #pragma unroll
@@ -943,8 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 tmem_wait_ld();
                                 if (b == C::kBoxes - 1 && h == 1) {
                                     tc_fence_before();
-                                    __syncwarp();
-                                    if (lane == 0) mbar_arrive(&o_empty[x]);
+                                    mbar_arrive(&o_empty[x]);
                                 }
                                 uint32_t pk[16];
 #pragma unroll
