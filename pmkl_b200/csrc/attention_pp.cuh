@@ -29,6 +29,13 @@
 //     do not wait for the tile's own maximum: they run against the reference
 //     of the earlier tiles while the maximum is gathered alongside, and the
 //     rare tile whose maximum lands far above that reference is redone.
+//   * hand-offs are kept short on each tile's chain: every softmax and epilogue
+//     thread arrives on the barriers it signals (no warp barrier and lane-0
+//     branch), warp-wide waits are tested by all 32 lanes (a vote, no
+//     broadcast from lane 0), the row-sum bookkeeping follows P's release,
+//     and at head size 128 the exps start once scores 0-31 are loaded.
+//   * the TMA warp pulls the next unit's Q and first K/V tiles into L2 a unit
+//     ahead (PMKL_PP_PREFETCH_NEXT).
 //   * every wait is bounded (sm100_ptx.cuh); on expiry the CTA drains its own
 //     copies and MMAs, frees tensor memory and reports PMKL_DEVERR_TIMEOUT.
 #pragma once
